@@ -1,0 +1,135 @@
+"""CPU oracle vs the committed golden fixtures (produced by the reference's
+own compiled preprocessing; see tests/golden/make_golden.py)."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from golden.make_golden import CASES, FUNCS, run_funcs
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def load_case(name):
+    z = np.load(GOLDEN / f"{name}.npz")
+    idt = torch.int32 if z["crow"].dtype == np.int32 else torch.int64
+    crow = torch.from_numpy(z["crow"]).to(idt)
+    col = torch.from_numpy(z["col"]).to(idt)
+    values = torch.from_numpy(z["values"])
+    dense = torch.from_numpy(z["dense"])
+    return z, int(z["nrows"]), int(z["ncols"]), crow, col, values, dense
+
+
+def as_bytes(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.uint8).numpy() if t.numel() else np.zeros(0, np.uint8)
+
+
+def expect_equal(golden: np.ndarray, got: torch.Tensor, key):
+    g = torch.from_numpy(np.ascontiguousarray(golden))
+    assert got.dtype == g.dtype, (key, got.dtype, g.dtype)
+    assert tuple(got.shape) == tuple(g.shape), (key, got.shape, g.shape)
+    assert np.array_equal(as_bytes(got), as_bytes(g)), key
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_layouts_match_golden(name):
+    z, nrows, ncols, crow, col, values, _ = load_case(name)
+    outs = run_funcs(oracle, nrows, ncols, crow, col, values)
+    for fn in FUNCS:
+        keys = {k.split("/", 1)[1] for k in z.files if k.startswith(fn + "/")}
+        assert keys == set(outs[fn].keys()), (fn, keys ^ set(outs[fn].keys()))
+        for k in keys:
+            expect_equal(z[f"{fn}/{k}"], outs[fn][k], f"{name}:{fn}/{k}")
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_spmm_matches_golden(name):
+    z, _, _, crow, col, values, dense = load_case(name)
+    y = oracle.spmm_csr_f64(crow, col, values, dense)
+    np.testing.assert_allclose(y, z["spmm_f64"], rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_mixed_semantics_reproduce_product(name):
+    """Every layout, fed to the mixed-operator semantics, reproduces A @ B
+    (preprocess in packed row order)."""
+    z, nrows, ncols, crow, col, values, dense = load_case(name)
+    ref = z["spmm_f64"]
+    for fn in ("block_level_split", "preprocess", "preprocess_graph"):
+        m = {k.split("/", 1)[1]: torch.from_numpy(np.ascontiguousarray(z[k]))
+             for k in z.files if k.startswith(fn + "/")}
+        y = oracle.spmm_mixed_f64(m["crow_window_ptr"], m["unique_col_ids"], m["value"],
+                                  m["vrow_window_ptr"], m["vcol_indices"], m["vvalue"], dense)
+        if fn.startswith("preprocess"):
+            perm = m["permutation"].numpy()
+            keep = perm >= 0
+            np.testing.assert_allclose(y[: perm.size][keep], ref[perm[keep]], rtol=1e-9, atol=1e-9)
+        else:
+            np.testing.assert_allclose(y[:nrows], ref, rtol=1e-9, atol=1e-9)
+    bc = {k.split("/", 1)[1]: torch.from_numpy(np.ascontiguousarray(z[k]))
+          for k in z.files if k.startswith("csr_to_bcsr/")}
+    empty_i = torch.zeros(1, dtype=torch.int64)
+    y = oracle.spmm_mixed_f64(bc["crow_window_ptr"], bc["unique_col_ids"], bc["value"],
+                              empty_i, torch.zeros(0, dtype=torch.int64),
+                              torch.zeros(0, dtype=values.dtype), dense)
+    np.testing.assert_allclose(y[:nrows], ref, rtol=1e-9, atol=1e-9)
+
+
+def test_oracle_graph_layout_identity():
+    """(P A P^T)(P B) = P (A B) for the relabelled forward layout, and the
+    fixed-layout transpose reproduces P A^T P^T."""
+    z, nrows, ncols, crow, col, values, dense = load_case("graph_i32_f16")
+    m = {k.split("/", 1)[1]: torch.from_numpy(np.ascontiguousarray(z[k]))
+         for k in z.files if k.startswith("preprocess_graph/")}
+    prow = int(m["packed_rows"][0])
+    inv = m["inv_permutation"].numpy()
+    perm = m["permutation"].numpy()
+    Bp = np.zeros((prow, dense.shape[1]))
+    Bp[inv] = dense.double().numpy()
+    y = oracle.spmm_mixed_f64(m["crow_window_ptr"], m["renumbered_unique_col_ids"], m["value"],
+                              m["vrow_window_ptr"], m["renumbered_vcol_indices"], m["vvalue"], Bp)
+    ref = z["spmm_f64"]
+    keep = perm >= 0
+    np.testing.assert_allclose(y[:prow][keep], ref[perm[keep]], rtol=1e-9, atol=1e-9)
+    # transpose: (P A^T P^T)(P B) = P (A^T B)
+    import scipy.sparse as sp
+    A = sp.csr_matrix((values.double().numpy(), col.numpy(), crow.numpy()), shape=(nrows, ncols))
+    refT = A.T @ dense.double().numpy()
+    yt = oracle.spmm_mixed_f64(m["transpose_crow_window_ptr"], m["transpose_unique_col_ids"],
+                               m["transpose_value"], m["transpose_vrow_window_ptr"],
+                               m["transpose_vcol_indices"], m["transpose_vvalue"], Bp)
+    np.testing.assert_allclose(yt[:prow][keep], refT[perm[keep]], rtol=1e-9, atol=1e-9)
+
+
+def test_oracle_empty_and_edge_inputs():
+    crow = torch.zeros(6, dtype=torch.int32)
+    col = torch.zeros(0, dtype=torch.int32)
+    val = torch.zeros(0, dtype=torch.float16)
+    d = oracle.csr_to_bcsr(crow, col, val, 5, 7, 16)
+    assert d["crow_window_ptr"].tolist() == [0, 0] and d["unique_col_ids"].numel() == 0
+    p = oracle.preprocess(crow, col, val, 5, 7, 16, False)
+    assert int(p["packed_rows"][0]) == 5 and p["vrow_window_ptr"].tolist() == [0] * 6
+    b = oracle.block_level_split(crow, col, val, 5, 7, 0.5, 16)
+    assert b["vrow_window_ptr"].numel() == 17
+    with pytest.raises(ValueError):
+        oracle.preprocess(crow, col, val, 5, 7, 8, False)
+    with pytest.raises(ValueError):
+        oracle.csr_to_bcsr(torch.tensor([0, 1], dtype=torch.int32), torch.tensor([9], dtype=torch.int32),
+                           torch.ones(1, dtype=torch.float16), 1, 7, 16)
+    # a column occupied more than 16 times in the marginal window (duplicate
+    # coordinates) makes the bucket sort throw, as in the reference
+    crow = torch.tensor([0, 17], dtype=torch.int32)
+    col = torch.full((17,), 3, dtype=torch.int32)
+    with pytest.raises(ValueError, match="coalesce"):
+        oracle.preprocess(crow, col, torch.ones(17, dtype=torch.float16), 1, 5, 16, False)
+
+
+def test_make_start_matches_reference_rule():
+    ptr = torch.tensor([0, 3, 3, 10, 11, 20], dtype=torch.int64)
+    s = oracle.make_start(ptr, 4)
+    # chunk = 5 -> targets 0,5,10,15 -> rows 0,2,3,4 (searchsorted right - 1)
+    assert s.tolist() == [0, 2, 3, 4]
+    assert oracle.make_start(torch.zeros(3, dtype=torch.int64), 4).tolist() == [0, 0, 0, 0]

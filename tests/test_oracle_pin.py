@@ -1,0 +1,76 @@
+"""Pin the C oracle to the reference's own compiled preprocessing on random
+inputs.  Runs where ``oracle/_ref`` exists (built by oracle/build_ref.py from
+the reference tree); skipped elsewhere, where the golden fixtures pin it."""
+
+import contextlib
+import io
+
+import numpy as np
+import pytest
+import torch
+
+import build_ref
+import oracle
+
+_REF = None
+
+
+def ref():
+    global _REF
+    if _REF is None:
+        _REF = build_ref.load() or False
+    if not _REF:
+        pytest.skip("reference preprocessing (oracle/_ref) not available")
+    return _REF
+
+
+def rand_csr(seed):
+    g = np.random.default_rng(seed)
+    nrows = int(g.integers(1, 160))
+    ncols = nrows if seed % 2 == 0 else int(g.integers(1, 160))
+    dens = float(g.uniform(0.0, 0.3))
+    rows = []
+    for r in range(nrows):
+        k = int(g.binomial(ncols, dens))
+        if seed % 3 == 0 and (r // 16) % 3 == 0:
+            k = min(ncols, k + int(g.integers(0, 20)))
+        rows.append(np.sort(g.choice(ncols, size=k, replace=False)))
+    crow = np.zeros(nrows + 1, np.int64)
+    crow[1:] = np.cumsum([len(c) for c in rows])
+    col = np.concatenate(rows) if rows else np.zeros(0, np.int64)
+    return nrows, ncols, crow, col
+
+
+def same(a: dict, b: dict):
+    assert set(a) == set(b)
+    for k in a:
+        x, y = a[k], b[k]
+        assert x.dtype == y.dtype and x.shape == y.shape, k
+        xb = x.view(torch.uint8) if x.is_floating_point() else x
+        yb = y.view(torch.uint8) if y.is_floating_point() else y
+        assert torch.equal(xb, yb), k
+
+
+@pytest.mark.parametrize("seed", range(24))
+def test_oracle_matches_reference(seed):
+    r = ref()
+    nrows, ncols, crow, col = rand_csr(seed)
+    if col.size == 0:
+        pytest.skip("the reference dereferences an empty column array")
+    idt = torch.int32 if seed % 4 < 2 else torch.int64
+    vdt = torch.float16 if seed % 2 == 0 else torch.float32
+    ct, cc = torch.from_numpy(crow).to(idt), torch.from_numpy(col).to(idt)
+    vals = (torch.rand(col.size, generator=torch.Generator().manual_seed(seed)) * 2 - 1).to(vdt)
+    with contextlib.redirect_stdout(io.StringIO()):
+        exp = {
+            "bcsr": r.csr_to_bcsr(ct, cc, vals, nrows, ncols, 16),
+            "cube": r.csr_to_ascend_cube(ct, cc, vals, nrows, ncols, 16),
+            "bls": r.block_level_split(ct, cc, vals, nrows, ncols, 0.584, 16),
+            "pre": r.preprocess(ct, cc, vals, nrows, ncols, 16, False),
+            "preg": r.preprocess(ct, cc, vals, nrows, ncols, 16, True),
+        }
+    same(oracle.csr_to_bcsr(ct, cc, vals, nrows, ncols, 16), exp["bcsr"])
+    same(oracle.csr_to_ascend_cube(ct, cc, vals, nrows, ncols, 16), exp["cube"])
+    same(oracle.block_level_split(ct, cc, vals, nrows, ncols, 0.584, 16), exp["bls"])
+    same(oracle.preprocess(ct, cc, vals, nrows, ncols, 16, False), exp["pre"])
+    same(oracle.preprocess(ct, cc, vals, nrows, ncols, 16, True), exp["preg"])
