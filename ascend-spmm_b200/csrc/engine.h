@@ -1,0 +1,88 @@
+// Internal host-side interface between the C ABI (capi.cu) and the kernel
+// translation units.  Not installed; the public ABI is include/spmm_b200.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace spmmb {
+
+struct DevStatus;
+
+// Per-device sticky status word (status.cu).
+DevStatus *device_status_ptr(cudaError_t *err);
+int device_sm_count();
+
+// ---- CSR gather path (gather.cu) ------------------------------------------
+
+// Work decomposition of one CSR gather launch: the nonzeros are cut into
+// equal units of `unit` positions; rows crossing a unit boundary are summed
+// from per-unit fp32 partials by a fix-up pass in unit order, so the result
+// is deterministic and independent of the grid.
+struct GatherPlan {
+    int64_t unit = 0;        // nonzeros per unit
+    int64_t unit_begin = 0;  // first unit index (absolute)
+    int64_t unit_end = 0;    // one past the last unit
+    int64_t N = 0;           // features
+    int64_t nunits() const { return unit_end - unit_begin; }
+    // fp32 head/tail partial rows, two per unit
+    size_t partial_bytes() const { return (size_t)nunits() * 2 * (size_t)N * sizeof(float); }
+};
+
+GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype);
+
+struct GatherArgs {
+    const void *rowptr;
+    const void *col;
+    const void *val;
+    const void *B;
+    void *out;
+    int64_t M;          // rows of the CSR (rowptr has M + 1 entries)
+    int64_t K;          // rows of B (valid column range)
+    int64_t N;          // features
+    int64_t nnz;
+    int64_t row_begin;  // rows below this are not written
+    int64_t unit;
+    int64_t unit_begin;
+    int64_t unit_end;
+    float *partial;     // (unit_end - unit_begin) * 2 * N floats
+    DevStatus *status;
+};
+
+// batch_depth: 0 = default gather batch, 1 = deeper batches (same sums).
+cudaError_t launch_gather(const GatherArgs &a, int itype, int dtype, int batch_depth,
+                          cudaStream_t stream);
+
+// ---- window path (window.cu) ----------------------------------------------
+
+struct WindowArgs {
+    const void *cptr;   // [nwin + 1] block offsets
+    const void *ccol;   // [nblocks]
+    const void *cval;   // [16 * nblocks]
+    const void *vptr;   // [vrows + 1]
+    const void *vcol;   // [vnnz]
+    const void *vval;   // [vnnz]
+    const void *B;
+    void *out;
+    int64_t nwin;
+    int64_t nblocks;
+    int64_t vrows;      // rows of the CSR part (only rows < 16 * nwin are fused here)
+    int64_t vnnz;
+    int64_t K;
+    int64_t N;
+    DevStatus *status;
+};
+
+// pipelined: 1 = multi-stage block stream (default), 0 = single stage.
+cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined,
+                          cudaStream_t stream);
+
+// ---- row permutation copies (rows.cu) ---------------------------------------
+
+cudaError_t launch_pack_rows(const void *src, const int64_t *inv, int64_t n, int64_t row_bytes, void *dst,
+                             int64_t packed_rows, DevStatus *st, cudaStream_t stream);
+cudaError_t launch_restore_rows(const void *src, int64_t src_rows, const int64_t *inv, int64_t n,
+                                int64_t row_bytes, void *dst, DevStatus *st, cudaStream_t stream);
+
+}  // namespace spmmb

@@ -1,0 +1,265 @@
+// CSR gather SpMM on CUDA cores (the sparse-row path).
+//
+// Semantics follow the reference's vector-core kernel
+// (kernels/op_kernel/spmm_csr.cpp:383-423): out[r, :] = sum_p val[p] * B[col[p], :]
+// with fp32 accumulation.  The B200 design is new:
+//
+//  * Work unit = a fixed range of `unit` nonzeros (not a row).  Units are
+//    dealt round-robin to resident warps, so a 4096-nonzero row costs the
+//    same per unit as 256 short rows and power-law skew cannot leave one
+//    warp with the tail.  The reference instead splits nnz statically over
+//    40 vector cores (op_host/spmm_csr.cpp:22-27).
+//  * A warp processes a unit as 32/G row lanes-groups of G lanes; a group
+//    owns one row at a time and each lane owns VPL 16-byte vectors of the
+//    row's N features, so every gathered B row is read with coalesced
+//    128-bit loads and U gathers per lane are kept in flight.
+//  * Each output element is a sequential fp32 fma chain over the row's
+//    nonzeros in CSR order.  A row crossing a unit boundary is accumulated
+//    per unit into an fp32 partial (head slot for the unit where it ends or
+//    continues, tail slot for the unit where it starts); csr_fixup_kernel sums
+//    the partials in unit order.  The split depends only on nnz, never on the
+//    grid, the feature width or the batching variant, so every variant is
+//    bitwise identical (the reference's AIV-variant tests demand this,
+//    tests/aic_aiv_ablation/bitwise_correctness.py:238-239) and no float
+//    atomics are used (the reference atomically adds fp16 partials at core
+//    boundaries, op_kernel/spmm_csr.cpp:472).
+//  * fp16 output is rounded to nearest once (the reference casts with
+//    round-toward-minus-infinity, spmm_csr.cpp:417).
+//  * Invalid column indices or row pointers are skipped and reported through
+//    the sticky device status instead of faulting.
+#include <algorithm>
+
+#include "../../include/spmm_b200.h"
+#include "common.cuh"
+#include "engine.h"
+
+namespace spmmb {
+
+namespace {
+
+constexpr int kGatherThreads = 256;
+
+// MINB: minimum resident blocks per SM requested from the register allocator
+// (3 x 256 threads = 24 warps/SM for the default batch of narrow rows).
+template <typename T, typename I, int G, int VPL, int U, int MINB>
+__global__ void __launch_bounds__(kGatherThreads, MINB)
+csr_gather_kernel(const GatherArgs a)
+{
+    constexpr int S = 32 / G;                   // row groups per warp
+    constexpr int EPV = Vec<T>::kElems;         // elements per 16-byte vector
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / G;
+    const int gl = lane % G;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+
+    const I *rowptr = static_cast<const I *>(a.rowptr);
+    const I *col = static_cast<const I *>(a.col);
+    const T *val = static_cast<const T *>(a.val);
+    const uint4 *B = static_cast<const uint4 *>(a.B);
+    const int NV = (int)(a.N / EPV);            // 16-byte vectors per row
+
+    for (int64_t u = a.unit_begin + warp; u < a.unit_end; u += nwarps) {
+        const int64_t lo = u * a.unit;
+        const int64_t hi = min(lo + a.unit, a.nnz);
+        const bool last = (u == a.unit_end - 1);
+        const int64_t i0 = warp_lower_bound(rowptr, a.row_begin, a.M + 1, lo);
+        int64_t r0 = i0;
+        if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r0 = i0 - 1;
+
+        for (int64_t r = r0 + sub; r < a.M; r += S) {
+            int64_t beg = ld_idx(rowptr + r);
+            int64_t end = ld_idx(rowptr + r + 1);
+            if (!(beg < hi || last)) break;
+            if (beg < 0 || end < beg || end > a.nnz) {
+                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                beg = end = max((int64_t)0, min(beg, a.nnz));
+            }
+            const int64_t sb = max(beg, lo);
+            const int n = (int)(min(end, hi) - sb);   // nonzeros of this row inside the unit
+            const I *cp = col + sb;
+            const T *vp = val + sb;
+
+            float acc[VPL][EPV];
+#pragma unroll
+            for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+
+            for (int p = 0; p < n; p += U) {
+                // Entries past the row or with an invalid column contribute
+                // fma(0, 0, acc); no per-entry predicate stays live.
+                uint4 b[U][VPL];
+                float v[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    int c = -1;
+                    v[j] = 0.f;
+                    if (p + j < n) {
+                        const int64_t cc = (int64_t)ld_stream(cp + p + j);
+                        if (cc >= 0 && cc < a.K) {
+                            c = (int)cc;
+                            v[j] = to_f32(ld_stream(vp + p + j));
+                        } else if (gl == 0) {
+                            raise_status(a.status, SPMM_DEV_BAD_COLUMN, sb + p + j);
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q) {
+                        const int vi = gl + q * G;
+                        b[j][q] = (c >= 0 && vi < NV) ? __ldg(B + (int64_t)c * NV + vi)
+                                                      : make_uint4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j)
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q) {
+                        float f[EPV];
+                        unpack16<T>(b[j][q], f);
+#pragma unroll
+                        for (int e = 0; e < EPV; ++e) acc[q][e] = fmaf(v[j], f[e], acc[q][e]);
+                    }
+            }
+
+            const bool head = beg < lo;
+            const bool tail = end > hi;
+            if (!head && !tail) {
+                uint4 *orow = static_cast<uint4 *>(a.out) + r * NV;
+#pragma unroll
+                for (int q = 0; q < VPL; ++q) {
+                    const int vi = gl + q * G;
+                    if (vi < NV) __stcs(orow + vi, pack16<T>(acc[q]));
+                }
+            } else {
+                float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
+#pragma unroll
+                for (int q = 0; q < VPL; ++q) {
+                    const int vi = gl + q * G;
+                    if (vi >= NV) continue;
+                    float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                    for (int e = 0; e < EPV; e += 4)
+                        dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                }
+            }
+        }
+    }
+}
+
+// Sums the per-unit partials of every row that crosses a unit boundary, in
+// unit order: tail(u0) + head(u0 + 1) + ... + head(u1).  One warp per unit;
+// a unit owns the fix-up of the split row that starts inside it.
+template <typename T, typename I>
+__global__ void __launch_bounds__(kGatherThreads)
+csr_fixup_kernel(const GatherArgs a)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const I *rowptr = static_cast<const I *>(a.rowptr);
+
+    for (int64_t u = a.unit_begin + warp; u < a.unit_end - 1; u += nwarps) {
+        const int64_t lo = u * a.unit;
+        const int64_t hi = lo + a.unit;
+        const int64_t i = warp_lower_bound(rowptr, a.row_begin, a.M + 1, hi);
+        const int64_t r = i - 1;
+        if (r < a.row_begin || r >= a.M) continue;
+        const int64_t beg = ld_idx(rowptr + r);
+        const int64_t end = ld_idx(rowptr + r + 1);
+        if (!(end > hi && beg >= lo && beg <= end && end <= a.nnz)) continue;
+        const int64_t u1 = min((end - 1) / a.unit, a.unit_end - 1);
+        for (int64_t f = (int64_t)lane * 4; f < a.N; f += 128) {
+            const float *base = a.partial + f;
+            float4 s = *reinterpret_cast<const float4 *>(base + ((u - a.unit_begin) * 2 + 1) * a.N);
+            for (int64_t w = u + 1; w <= u1; ++w) {
+                const float4 h = *reinterpret_cast<const float4 *>(base + ((w - a.unit_begin) * 2) * a.N);
+                s.x += h.x; s.y += h.y; s.z += h.z; s.w += h.w;
+            }
+            T *o = static_cast<T *>(a.out) + r * a.N + f;
+            if constexpr (sizeof(T) == 2) {
+                __half2 *o2 = reinterpret_cast<__half2 *>(o);
+                o2[0] = __floats2half2_rn(s.x, s.y);
+                o2[1] = __floats2half2_rn(s.z, s.w);
+            } else {
+                *reinterpret_cast<float4 *>(o) = s;
+            }
+        }
+    }
+}
+
+template <typename T, typename I, int G, int VPL, int U, int MINB>
+cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
+{
+    auto kern = csr_gather_kernel<T, I, G, VPL, U, MINB>;
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGatherThreads, 0);
+    if (e != cudaSuccess) return e;
+    const int64_t warps_needed = a.unit_end - a.unit_begin;
+    int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
+    blocks = std::min(blocks, (warps_needed + 7) / 8);
+    blocks = std::max<int64_t>(blocks, 1);
+    kern<<<(unsigned)blocks, kGatherThreads, 0, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (a.unit_end - a.unit_begin > 1) {
+        const int64_t fb = std::min<int64_t>((warps_needed + 7) / 8, 8LL * device_sm_count());
+        csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+// U x VPL = 8 sixteen-byte gathers in flight per lane (128 B) at 24 warps/SM
+// by default; the deep-batch variant keeps 16 in flight at 16 warps/SM.
+// Both consume the nonzeros of a row in the same order, so their sums are
+// bitwise identical.
+template <typename T, typename I>
+cudaError_t launch_typed(const GatherArgs &a, int batch_depth, cudaStream_t s)
+{
+    const int64_t NV = a.N / Vec<T>::kElems;
+    const bool deep = batch_depth != 0;
+#define SPMM_GATHER_CFG(G, VPL, U)                                                        \
+    return deep ? launch_cfg<T, I, G, VPL, 2 * (U), ((VPL) > 1 ? 1 : 2)>(a, s)              \
+                : launch_cfg<T, I, G, VPL, U, ((VPL) > 1 ? 2 : 3)>(a, s)
+    if (NV <= 2) SPMM_GATHER_CFG(2, 1, 8);
+    if (NV <= 4) SPMM_GATHER_CFG(4, 1, 8);
+    if (NV <= 8) SPMM_GATHER_CFG(8, 1, 8);
+    if (NV <= 16) SPMM_GATHER_CFG(16, 1, 8);
+    if (NV <= 32) SPMM_GATHER_CFG(32, 1, 8);
+    if (NV <= 64) SPMM_GATHER_CFG(32, 2, 4);
+    SPMM_GATHER_CFG(32, 4, 2);
+#undef SPMM_GATHER_CFG
+}
+
+}  // namespace
+
+GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype)
+{
+    (void)dtype;
+    GatherPlan p;
+    p.N = N;
+    // Unit size depends on nnz only (never on N, the device or the variant):
+    // about 32K units, 256..8192 nonzeros each, a power of two.
+    int64_t target = (nnz + 32767) / 32768;
+    int64_t unit = 256;
+    while (unit < target && unit < 8192) unit <<= 1;
+    p.unit = unit;
+    p.unit_begin = 0;
+    p.unit_end = std::max<int64_t>(1, (nnz + unit - 1) / unit);
+    return p;
+}
+
+cudaError_t launch_gather(const GatherArgs &a, int itype, int dtype, int batch_depth,
+                          cudaStream_t stream)
+{
+    if (a.M <= a.row_begin) return cudaSuccess;
+    if (dtype == SPMM_F16) {
+        return itype == SPMM_I32 ? launch_typed<__half, int>(a, batch_depth, stream)
+                                 : launch_typed<__half, int64_t>(a, batch_depth, stream);
+    }
+    return itype == SPMM_I32 ? launch_typed<float, int>(a, batch_depth, stream)
+                             : launch_typed<float, int64_t>(a, batch_depth, stream);
+}
+
+}  // namespace spmmb

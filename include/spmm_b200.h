@@ -1,0 +1,158 @@
+/*
+ * spmm_b200.h - C ABI of the B200 SpMM engine (libspmm_b200.so).
+ *
+ * Plain pointers, sizes and status codes; no framework types.  Every SpMM
+ * entry point mirrors one operator of the reference's `spmm_npu` module
+ * (IDMG-Lab/Ascend-SpMM, extension/custom_op.cpp) and is what an FFI
+ * binding of that operator calls.  Citations are path:line in the
+ * reference project.
+ *
+ * Conventions
+ *   - All array pointers are DEVICE pointers on the current CUDA device,
+ *     contiguous, unless stated otherwise.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *     Launches are asynchronous on that stream, like the reference's
+ *     EXEC_NPU_CMD on the current NPU stream (pytorch_npu_helper.hpp:516-581).
+ *   - Index arrays are int32 (SPMM_I32) or int64 (SPMM_I64): the reference
+ *     registers both index types (kernels/op_host/spmm_ascend_cube.cpp:77-126).
+ *   - Value/dense/output dtype is SPMM_F16 or SPMM_F32; products accumulate
+ *     in fp32 and the fp16 output is rounded to nearest once.
+ *   - The `start` arrays of the reference ops (per-core first rows,
+ *     tests/task_mapping/common.py:119-127) are accepted for signature
+ *     compatibility and ignored: the engine plans its own nnz-balanced split.
+ *   - Ops that need scratch take a caller-provided device workspace whose
+ *     size the matching *_workspace_bytes() reports; they allocate nothing.
+ *   - Output arrays are fully written by the launch (no pre-zeroing needed).
+ *   - Invalid indices found on the device never fault: the entry is skipped
+ *     and a sticky device status is raised (spmm_device_status()).
+ *
+ * Return value: SPMM_OK or an SPMM_ERR_* code; spmm_last_error() gives a
+ * message (thread-local, valid until the next call on the same thread).
+ */
+#ifndef SPMM_B200_H_
+#define SPMM_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum spmm_status {
+    SPMM_OK = 0,
+    SPMM_ERR_ARG = 1,          /* invalid argument (shape, dtype, contract) */
+    SPMM_ERR_CUDA = 2,         /* a CUDA runtime call failed */
+    SPMM_ERR_DEVICE_CHECK = 3, /* device-side validation found invalid data */
+    SPMM_ERR_UNSUPPORTED = 4,  /* valid request this build does not serve */
+    SPMM_ERR_ALLOC = 5,        /* the caller's allocator returned NULL */
+    SPMM_ERR_WORKSPACE = 6     /* workspace smaller than *_workspace_bytes() */
+};
+
+enum spmm_dtype { SPMM_F16 = 0, SPMM_F32 = 1, SPMM_F64 = 2 };
+enum spmm_itype { SPMM_I32 = 0, SPMM_I64 = 1 };
+
+/* Device-status codes raised by kernels (see spmm_device_status). */
+enum spmm_device_code {
+    SPMM_DEV_OK = 0,
+    SPMM_DEV_BAD_COLUMN = 1,   /* a column index outside [0, K) was skipped */
+    SPMM_DEV_BAD_ROWPTR = 2,   /* a row pointer was non-monotone or > nnz */
+    SPMM_DEV_UNSORTED = 3,     /* a row's columns are not strictly ascending */
+    SPMM_DEV_OCCUPANCY = 4,    /* a block column occupied > window_size times */
+    SPMM_DEV_TIMEOUT = 5       /* a bounded device wait gave up */
+};
+
+const char *spmm_last_error(void);
+int spmm_abi_version(void);
+
+/* Sticky device status of the current device: first error code and a detail
+ * value (the offending position).  Synchronises `stream`.  With reset != 0
+ * the status is cleared after reading. */
+int spmm_device_status(int *code, int64_t *detail, int reset, void *stream);
+
+/* ---------------------------------------------------------------------- */
+/* CSR SpMM: out[M, N] = A[M, K] * dense[K, N].                            */
+/* Replaces spmm_csr_impl_npu (extension/custom_op.cpp:67-88; kernel       */
+/* kernels/op_kernel/spmm_csr.cpp:226-569).  Width contract: fp16 N % 16,  */
+/* N <= 1024; fp32 N % 8, N <= 512 (custom_op.cpp:39-57).                   */
+/* ---------------------------------------------------------------------- */
+size_t spmm_csr_workspace_bytes(int64_t M, int64_t N, int64_t nnz, int dtype);
+
+int spmm_csr_launch(const void *rowptr, const void *col, const void *value,
+                    const void *dense, const int32_t *start, int64_t n_start,
+                    void *out, int64_t M, int64_t K, int64_t N, int64_t nnz,
+                    int itype, int dtype, void *workspace, size_t workspace_bytes,
+                    void *stream);
+
+/* Replaces spmm_csr_aiv_mb_batch_impl_npu (custom_op.cpp:154-187; kernel
+ * kernels/op_kernel/spmm_csr_aiv_mb_batch.cpp).  Same math and the same
+ * nnz split as spmm_csr_launch (bitwise-identical output); it issues its
+ * gathers in deeper batches.  Same workspace. */
+int spmm_csr_aiv_mb_batch_launch(const void *rowptr, const void *col, const void *value,
+                                 const void *dense, const int32_t *start, int64_t n_start,
+                                 void *out, int64_t M, int64_t K, int64_t N, int64_t nnz,
+                                 int itype, int dtype, void *workspace,
+                                 size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------- */
+/* Mixed window/CSR SpMM.  Output rows = max(16 * n_windows, v_rows)       */
+/* (custom_op.cpp:146).  Window slot s adds its (16 x 1)-block products to  */
+/* rows [16s, 16s + 16); the CSR part adds to its own rows; both parts are */
+/* summed in fp32 before a single rounding.                                */
+/* Replaces spmm_ascend_cube_impl_npu (custom_op.cpp:115-152; kernel        */
+/* kernels/op_kernel/spmm_ascend_cube.cpp:887-907).  N % 16 == 0.           */
+/*   Crowptr  [n_windows + 1]  block offsets per window                     */
+/*   Ccol_ids [n_blocks]       block column ids                             */
+/*   Cvalue   [16 * n_blocks]  Cvalue[16 b + i] = A[row i of window, col b] */
+/*   Vrowptr  [v_rows + 1], Vcol_ids [v_nnz], Vvalue [v_nnz]                */
+/* ---------------------------------------------------------------------- */
+size_t spmm_ascend_cube_workspace_bytes(int64_t n_windows, int64_t n_blocks, int64_t v_rows,
+                                        int64_t v_nnz, int64_t N, int dtype);
+
+int spmm_ascend_cube_launch(const void *Crowptr, const void *Ccol_ids, const void *Cvalue,
+                            const void *Vrowptr, const void *Vcol_ids, const void *Vvalue,
+                            const void *dense, const int32_t *Cstart, int64_t n_cstart,
+                            const int32_t *Vstart, int64_t n_vstart, void *out,
+                            int64_t n_windows, int64_t n_blocks, int64_t v_rows, int64_t v_nnz,
+                            int64_t K, int64_t N, int itype, int dtype, void *workspace,
+                            size_t workspace_bytes, void *stream);
+
+/* Replaces spmm_ascend_cube_aic_without_pipeline_impl_npu (custom_op.cpp:
+ * 189-245): the window path with a single-stage (unpipelined) block stream,
+ * the analogue of the reference's SPTILE=16 ablation. Same arguments. */
+int spmm_ascend_cube_aic_without_pipeline_launch(
+    const void *Crowptr, const void *Ccol_ids, const void *Cvalue, const void *Vrowptr,
+    const void *Vcol_ids, const void *Vvalue, const void *dense, const int32_t *Cstart,
+    int64_t n_cstart, const int32_t *Vstart, int64_t n_vstart, void *out, int64_t n_windows,
+    int64_t n_blocks, int64_t v_rows, int64_t v_nnz, int64_t K, int64_t N, int itype,
+    int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Replaces spmm_ascend_cube_aiv_mb_impl_npu (custom_op.cpp:247-264): the CSR
+ * part with deeper gather batching (bitwise-identical CSR results). */
+int spmm_ascend_cube_aiv_mb_launch(
+    const void *Crowptr, const void *Ccol_ids, const void *Cvalue, const void *Vrowptr,
+    const void *Vcol_ids, const void *Vvalue, const void *dense, const int32_t *Cstart,
+    int64_t n_cstart, const int32_t *Vstart, int64_t n_vstart, void *out, int64_t n_windows,
+    int64_t n_blocks, int64_t v_rows, int64_t v_nnz, int64_t K, int64_t N, int itype,
+    int dtype, void *workspace, size_t workspace_bytes, void *stream);
+
+/* ---------------------------------------------------------------------- */
+/* Graph-layout row permutation (P and P^T on node tensors).               */
+/* ---------------------------------------------------------------------- */
+
+/* Replaces pack_node_tensor (spmm_npu.py:22-47): dst[inv[i], :] = src[i, :]
+ * for i < n; all other of the packed_rows rows of dst are zeroed.  Rows are
+ * row_bytes bytes; inv is int64 on the device. */
+int spmm_pack_rows_launch(const void *src, const int64_t *inv, int64_t n, int64_t row_bytes, void *dst,
+                          int64_t packed_rows, void *stream);
+
+/* Replaces restore_node_tensor (spmm_npu.py:50-61): dst[i, :] = src[inv[i], :]
+ * for i < n; src has src_rows rows. */
+int spmm_restore_rows_launch(const void *src, int64_t src_rows, const int64_t *inv, int64_t n,
+                             int64_t row_bytes, void *dst, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPMM_B200_H_ */

@@ -1,0 +1,83 @@
+"""CPU checks of the drop-in boundary: the C-ABI library loads and exports
+every entry point include/spmm_b200.h declares; the torch-facing module
+imports and exposes the reference's operator names.  No compute (no GPU)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+PKG = ROOT / "ascend-spmm_b200"
+
+
+def declared_functions():
+    text = (ROOT / "include" / "spmm_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(spmm_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build
+
+    build.build_lib()
+    return ctypes.CDLL(str(build.LIB))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("spmm_csr_launch", "spmm_ascend_cube_launch", "spmm_csr_workspace_bytes",
+              "spmm_device_status", "spmm_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_workspace_queries(lib):
+    assert lib.spmm_abi_version() == 1
+    lib.spmm_csr_workspace_bytes.restype = ctypes.c_size_t
+    lib.spmm_csr_workspace_bytes.argtypes = [ctypes.c_int64] * 3 + [ctypes.c_int]
+    # 163840 nonzeros -> 640 units of 256, two fp32 partial rows of N=128 each
+    assert lib.spmm_csr_workspace_bytes(16384, 128, 163840, 0) == 640 * 2 * 128 * 4
+
+
+def test_argument_errors_need_no_gpu(lib):
+    """Contract violations are rejected on the host with the reference's text."""
+    lib.spmm_csr_launch.restype = ctypes.c_int
+    lib.spmm_last_error.restype = ctypes.c_char_p
+    V = ctypes.c_void_p
+    i64 = ctypes.c_int64
+    lib.spmm_csr_launch.argtypes = [V, V, V, V, V, i64, V, i64, i64, i64, i64, ctypes.c_int, ctypes.c_int,
+                                    V, ctypes.c_size_t, V]
+    rc = lib.spmm_csr_launch(None, None, None, None, None, 0, None, 4, 4, 24, 0, 0, 0, None, 0, None)
+    assert rc == 1
+    assert b"feature width divisible by 16, but got 24" in lib.spmm_last_error()
+    rc = lib.spmm_csr_launch(None, None, None, None, None, 0, None, 4, 4, 1040, 0, 0, 0, None, 0, None)
+    assert rc == 1 and b"0 < feature width <= 1024 for FP16" in lib.spmm_last_error()
+
+
+def test_torch_module_exposes_reference_names():
+    import build
+
+    build.build()
+    import spmm_npu
+
+    for name in ("block_level_split", "csr_to_ascend_cube", "csr_to_bcsr", "pack_node_tensor", "preprocess",
+                 "restore_node_tensor", "spmm_ascend_cube", "spmm_ascend_cube_aic_without_pipeline",
+                 "spmm_ascend_cube_aiv_mb", "spmm_csr", "spmm_csr_aiv_mb_batch", "spmm_cube"):
+        assert name in spmm_npu.__all__
+
+
+def test_operators_reject_cpu_tensors():
+    import torch
+
+    import spmm_npu
+
+    x = torch.zeros(2, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="must be CUDA tensor"):
+        spmm_npu.spmm_csr(x, x[:0], torch.zeros(0, dtype=torch.float16), torch.zeros(4, 16, dtype=torch.float16), x)

@@ -1,0 +1,264 @@
+"""GPU parity of the SpMM operators against the float64 CPU oracle.
+
+Tolerances are the reference's (fp16 2e-2, fp32 1e-4,
+tests/task_mapping/correctness.py:140-143); CUDA-core variants must agree
+bitwise (tests/aic_aiv_ablation/bitwise_correctness.py:238-239).  All calls
+go through ``spmm_npu`` -> ``custom_ops_lib`` -> the C ABI of
+libspmm_b200.so.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from golden.make_golden import CASES
+from helpers import assert_close, golden_layout, load_golden, rand_csr
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def npu():
+    import build
+
+    build.build()
+    import spmm_npu
+
+    assert torch.cuda.is_available()
+    return spmm_npu
+
+
+def start_of(ptr, cores):
+    return oracle.make_start(ptr.cpu().to(torch.int64), cores).to(DEV)
+
+
+def csr_call(npu, crow, col, val, B, op="spmm_csr"):
+    return getattr(npu, op)(crow.to(DEV), col.to(DEV), val.to(DEV), B.to(DEV), start_of(crow, 40))
+
+
+def mixed_call(npu, m, B, op="spmm_ascend_cube", cols_key="unique_col_ids", vcols_key="vcol_indices"):
+    args = [m["crow_window_ptr"], m[cols_key], m["value"], m["vrow_window_ptr"], m[vcols_key], m["vvalue"]]
+    args = [a.to(DEV) for a in args]
+    return getattr(npu, op)(*args, B.to(DEV), start_of(m["crow_window_ptr"], 20),
+                            start_of(m["vrow_window_ptr"], 40))
+
+
+def check_status(npu):
+    code, detail = npu.device_status(True)
+    assert code == 0, f"device status {code} at {detail}"
+
+
+# ---------------------------------------------------------------- spmm_csr
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_spmm_csr_golden(npu, name):
+    c = load_golden(name)
+    y = csr_call(npu, c["crow"], c["col"], c["values"], c["dense"])
+    torch.cuda.synchronize()
+    assert y.dtype == c["values"].dtype and y.shape == (c["nrows"], c["dense"].shape[1])
+    assert_close(y, c["z"]["spmm_f64"], y.dtype, name)
+    check_status(npu)
+
+
+@pytest.mark.parametrize("dtype,N", [(torch.float16, w) for w in (16, 32, 48, 64, 128, 256, 512, 1024)]
+                         + [(torch.float32, w) for w in (8, 24, 64, 256, 512)])
+def test_spmm_csr_widths(npu, dtype, N):
+    M, K = 700, 523
+    crow, col = rand_csr(M, K, 0.03, seed=N, long_rows={5: 400, 333: 520}, empty_every=7)
+    g = torch.Generator().manual_seed(N)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
+    B = torch.randn(K, N, generator=g).to(dtype)
+    y = csr_call(npu, crow, col, val, B)
+    assert_close(y, oracle.spmm_csr_f64(crow, col, val, B), dtype, f"N={N}")
+    check_status(npu)
+
+
+@pytest.mark.parametrize("idt", [torch.int32, torch.int64])
+def test_spmm_csr_long_rows_cross_many_units(npu, idt):
+    """Rows much longer than a unit are split across units and re-summed by
+    the fix-up pass; includes a row spanning > 20 units and empty rows at
+    unit boundaries."""
+    M, K = 64, 9000
+    crow, col = rand_csr(M, K, 0.01, seed=3, long_rows={0: 6000, 10: 300, 63: 8000}, empty_every=5, idt=idt)
+    g = torch.Generator().manual_seed(1)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).half()
+    B = torch.randn(K, 64, generator=g).half()
+    y = csr_call(npu, crow, col, val, B)
+    assert_close(y, oracle.spmm_csr_f64(crow, col, val, B), torch.float16)
+    check_status(npu)
+
+
+def test_spmm_csr_edge_shapes(npu):
+    # no nonzeros at all: every row is zero
+    crow = torch.zeros(33, dtype=torch.int32)
+    y = csr_call(npu, crow, torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.float16),
+                 torch.randn(8, 16).half())
+    assert y.shape == (32, 16) and not bool(y.any())
+    # zero rows
+    y = csr_call(npu, torch.zeros(1, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                 torch.zeros(0, dtype=torch.float16), torch.randn(8, 16).half())
+    assert y.shape == (0, 16)
+    # single nonzero
+    y = csr_call(npu, torch.tensor([0, 1], dtype=torch.int32), torch.tensor([3], dtype=torch.int32),
+                 torch.tensor([0.5], dtype=torch.float16), torch.arange(64).reshape(4, 16).half())
+    assert torch.equal(y.cpu(), (0.5 * torch.arange(48, 64)).half().reshape(1, 16))
+    check_status(npu)
+
+
+def test_variants_bitwise_identical(npu):
+    """All CUDA-core variants share one nnz split and one per-element fma
+    order: spmm_csr == spmm_csr_aiv_mb_batch == pure-CSR spmm_ascend_cube ==
+    spmm_ascend_cube_aiv_mb, for every width."""
+    M, K = 2000, 1500
+    crow, col = rand_csr(M, K, 0.01, seed=11, long_rows={7: 1200, 1999: 900}, empty_every=13)
+    g = torch.Generator().manual_seed(5)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).half()
+    empty = {"crow_window_ptr": torch.zeros(1, dtype=torch.int32),
+             "unique_col_ids": torch.zeros(0, dtype=torch.int32),
+             "value": torch.zeros(0, dtype=torch.float16),
+             "vrow_window_ptr": crow, "vcol_indices": col, "vvalue": val}
+    for N in (16, 32, 64, 128, 256):
+        B = torch.randn(K, N, generator=g).half()
+        ref = csr_call(npu, crow, col, val, B)
+        for other in (csr_call(npu, crow, col, val, B, "spmm_csr_aiv_mb_batch"),
+                      mixed_call(npu, empty, B)[:M],
+                      mixed_call(npu, empty, B, "spmm_ascend_cube_aiv_mb")[:M]):
+            assert torch.equal(other, ref), N
+    check_status(npu)
+
+
+# --------------------------------------------------------- mixed operator
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+@pytest.mark.parametrize("layout", ["block_level_split", "preprocess", "preprocess_graph", "csr_to_bcsr"])
+def test_mixed_golden_layouts(npu, name, layout):
+    """The reference's own layouts (golden fixtures) fed to spmm_ascend_cube
+    reproduce A @ B; preprocess layouts in packed row order."""
+    c = load_golden(name)
+    m = golden_layout(c, layout)
+    dtype = c["values"].dtype
+    if layout == "csr_to_bcsr":
+        m.update(vrow_window_ptr=torch.zeros(1, dtype=m["crow_window_ptr"].dtype),
+                 vcol_indices=torch.zeros(0, dtype=m["crow_window_ptr"].dtype),
+                 vvalue=torch.zeros(0, dtype=dtype))
+    B = c["dense"]
+    ref = c["z"]["spmm_f64"]
+    for op in ("spmm_ascend_cube", "spmm_ascend_cube_aic_without_pipeline", "spmm_ascend_cube_aiv_mb"):
+        y = mixed_call(npu, m, B, op)
+        nwin = m["crow_window_ptr"].numel() - 1
+        assert y.shape[0] == max(16 * nwin, m["vrow_window_ptr"].numel() - 1)
+        if layout.startswith("preprocess"):
+            perm = m["permutation"].numpy()
+            keep = perm >= 0
+            assert_close(y[: perm.size].cpu()[torch.from_numpy(keep)], ref[perm[keep]], dtype, f"{name}/{layout}/{op}")
+        else:
+            assert_close(y[: c["nrows"]], ref, dtype, f"{name}/{layout}/{op}")
+    check_status(npu)
+
+
+def test_mixed_graph_layout_relabelled(npu):
+    """(P A P^T)(P B) = P (A B) through the renumbered forward layout, and the
+    fixed-layout transpose gives P (A^T B)."""
+    c = load_golden("graph_i32_f16")
+    m = golden_layout(c, "preprocess_graph")
+    inv = m["inv_permutation"]
+    prow = int(m["packed_rows"][0])
+    Bp = npu.pack_node_tensor(c["dense"].to(DEV), inv.to(DEV), prow)
+    y = mixed_call(npu, m, Bp, cols_key="renumbered_unique_col_ids", vcols_key="renumbered_vcol_indices")
+    restored = npu.restore_node_tensor(y, inv.to(DEV))
+    assert_close(restored, c["z"]["spmm_f64"], torch.float16, "forward")
+    t = {k[len("transpose_"):]: v for k, v in m.items() if k.startswith("transpose_")}
+    yt = mixed_call(npu, t, Bp)
+    import scipy.sparse as sp
+    A = sp.csr_matrix((c["values"].double().numpy(), c["col"].numpy(), c["crow"].numpy()),
+                      shape=(c["nrows"], c["ncols"]))
+    refT = A.T @ c["dense"].double().numpy()
+    assert_close(npu.restore_node_tensor(yt, inv.to(DEV)), refT, torch.float16, "transpose")
+    check_status(npu)
+
+
+@pytest.mark.parametrize("dtype,N", [(torch.float16, 16), (torch.float16, 272), (torch.float16, 1024),
+                                     (torch.float32, 16), (torch.float32, 512)])
+def test_mixed_random_windows(npu, dtype, N):
+    """Windows with many blocks (several pipeline chunks), CSR rows fused into
+    every window, and CSR rows beyond the window region."""
+    g = np.random.default_rng(N)
+    nwin, K = 9, 700
+    nb = g.integers(0, 80, nwin)
+    nb[3] = 0
+    cptr = torch.from_numpy(np.concatenate([[0], np.cumsum(nb)])).to(torch.int32)
+    ccol = torch.from_numpy(np.concatenate([np.sort(g.choice(K, int(n), replace=False)) for n in nb])).to(torch.int32)
+    gen = torch.Generator().manual_seed(N)
+    cval = (torch.rand(16 * int(nb.sum()), generator=gen) * 2 - 1).to(dtype)
+    cval[torch.rand(cval.numel(), generator=gen) < 0.4] = 0
+    vrows = 16 * nwin + 37
+    vcrow, vcol = rand_csr(vrows, K, 0.02, seed=N, long_rows={20: 300, 16 * nwin + 3: 500}, empty_every=4)
+    vval = (torch.rand(vcol.numel(), generator=gen) * 2 - 1).to(dtype)
+    B = torch.randn(K, N, generator=gen).to(dtype)
+    m = {"crow_window_ptr": cptr, "unique_col_ids": ccol, "value": cval,
+         "vrow_window_ptr": vcrow, "vcol_indices": vcol, "vvalue": vval}
+    ref = oracle.spmm_mixed_f64(cptr, ccol, cval, vcrow, vcol, vval, B)
+    for op in ("spmm_ascend_cube", "spmm_ascend_cube_aic_without_pipeline", "spmm_ascend_cube_aiv_mb"):
+        assert_close(mixed_call(npu, m, B, op), ref, dtype, op)
+    check_status(npu)
+
+
+# ------------------------------------------------------ failure handling
+
+def test_invalid_columns_are_reported_not_faulted(npu):
+    npu.device_status(True)
+    crow = torch.tensor([0, 2, 3], dtype=torch.int32)
+    col = torch.tensor([1, 99, 0], dtype=torch.int32)   # 99 >= K
+    val = torch.ones(3, dtype=torch.float16)
+    B = torch.ones(4, 16, dtype=torch.float16)
+    y = csr_call(npu, crow, col, val, B)
+    code, detail = npu.device_status(True)
+    assert code == 1 and detail == 1
+    assert torch.equal(y.cpu(), torch.ones(2, 16, dtype=torch.float16))
+    # a row pointer past nnz is clamped and reported
+    crow = torch.tensor([0, 2, 9], dtype=torch.int32)
+    y = csr_call(npu, crow, col, val, B)
+    code, _ = npu.device_status(True)
+    assert code == 2
+
+
+def test_contract_errors(npu):
+    crow = torch.tensor([0, 1], dtype=torch.int32, device=DEV)
+    col = torch.tensor([0], dtype=torch.int32, device=DEV)
+    v = torch.ones(1, dtype=torch.float16, device=DEV)
+    s = torch.zeros(40, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="feature width divisible by 16"):
+        npu.spmm_csr(crow, col, v, torch.ones(2, 24, dtype=torch.float16, device=DEV), s)
+    with pytest.raises(RuntimeError, match="0 < feature width <= 512 for FP32"):
+        npu.spmm_csr(crow, col, v.float(), torch.ones(2, 520, device=DEV), s)
+    with pytest.raises(RuntimeError, match="value must have the same dtype as dense"):
+        npu.spmm_csr(crow, col, v, torch.ones(2, 16, device=DEV), s)
+    with pytest.raises(RuntimeError, match="col and value must be same size"):
+        npu.spmm_csr(crow, col, torch.ones(2, dtype=torch.float16, device=DEV),
+                     torch.ones(2, 16, dtype=torch.float16, device=DEV), s)
+    with pytest.raises(RuntimeError, match="requires a contiguous dense tensor"):
+        npu.spmm_csr(crow, col, v, torch.ones(16, 2, dtype=torch.float16, device=DEV).t(), s)
+    z = torch.zeros(1, dtype=torch.int32, device=DEV)
+    with pytest.raises(RuntimeError, match="spmm_ascend_cube requires feature width divisible by 16"):
+        npu.spmm_ascend_cube(z, z[:0], v[:0], crow, col, v.float(), torch.ones(2, 8, device=DEV), s, s)
+
+
+# ------------------------------------------------------ pack / restore
+
+def test_pack_restore_roundtrip(npu):
+    n = 37
+    inv = torch.randperm(48, generator=torch.Generator().manual_seed(0))[:n]
+    for x in (torch.randn(n, 5), torch.randn(n, 16).half(), torch.arange(n, dtype=torch.int64)):
+        xp = npu.pack_node_tensor(x.to(DEV), inv.to(DEV), 48)
+        assert xp.shape[0] == 48
+        ref = torch.zeros((48, *x.shape[1:]), dtype=x.dtype)
+        ref.index_copy_(0, inv, x)
+        assert torch.equal(xp.cpu(), ref)
+        assert torch.equal(npu.restore_node_tensor(xp, inv.to(DEV)).cpu(), x)
+    with pytest.raises(ValueError, match="smaller than the permutation extent"):
+        npu.pack_node_tensor(torch.zeros(n, 2, device=DEV), inv.to(DEV), 10)
+    with pytest.raises(ValueError, match="one entry per original node"):
+        npu.pack_node_tensor(torch.zeros(n + 1, 2, device=DEV), inv.to(DEV))
