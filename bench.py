@@ -49,8 +49,8 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=30)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", type=int, default=2)
     p.add_argument("--scale", type=float, default=1.0)
@@ -142,7 +142,7 @@ class ClockSampler:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self

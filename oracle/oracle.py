@@ -303,7 +303,8 @@ def spmm_mixed_f64(Crowptr, Ccol_ids, Cvalue, Vrowptr, Vcol_ids, Vvalue, dense) 
 
 def cpu_reference(rows, cols, crow, col, values, dense) -> torch.Tensor:
     """tests/aic_aiv_ablation/common.py:173-177 restated: torch.sparse.mm in fp32."""
-    matrix = torch.sparse_csr_tensor(crow, col, values.float(), size=(rows, cols))
+    matrix = torch.sparse_csr_tensor(crow, col, values.float(), size=(rows, cols),
+                                     check_invariants=False)
     return torch.sparse.mm(matrix, dense.float())
 
 
