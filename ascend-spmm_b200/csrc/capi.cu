@@ -149,6 +149,19 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
 
 }  // namespace
 
+namespace spmmb {
+int capi_error(int code, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+}  // namespace spmmb
+
 extern "C" {
 
 const char *spmm_last_error(void) { return g_last_error.c_str(); }
@@ -236,6 +249,38 @@ int spmm_ascend_cube_aiv_mb_launch(SPMM_MIXED_ARGS)
 {
     (void)Cstart; (void)n_cstart; (void)Vstart; (void)n_vstart;
     return mixed_impl(SPMM_MIXED_FORWARD, 1, 1, "spmm_ascend_cube_aiv_mb");
+}
+
+int spmm_csr_to_bcsr_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                         int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
+                         spmm_layout *out, void *stream)
+{
+    return spmmb::pre_csr_to_bcsr(crow, col, val, nrows, ncols, nnz, window_size, itype, vbytes, alloc, out, stream,
+                                  false);
+}
+
+int spmm_csr_to_ascend_cube_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                                int64_t nnz, int64_t window_size, int itype, int vbytes,
+                                const spmm_allocator *alloc, spmm_layout *out, void *stream)
+{
+    return spmmb::pre_csr_to_bcsr(crow, col, val, nrows, ncols, nnz, window_size, itype, vbytes, alloc, out, stream,
+                                  true);
+}
+
+int spmm_block_level_split_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                               int64_t nnz, double a, int64_t window_size, int itype, int vbytes,
+                               const spmm_allocator *alloc, spmm_layout *out, void *stream)
+{
+    return spmmb::pre_block_level_split(crow, col, val, nrows, ncols, nnz, a, window_size, itype, vbytes, alloc,
+                                        out, stream);
+}
+
+int spmm_preprocess_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                        int64_t nnz, int64_t window_size, int graph_layout, int itype, int vbytes,
+                        const spmm_allocator *alloc, spmm_preprocess_result *out, void *stream)
+{
+    return spmmb::pre_preprocess(crow, col, val, nrows, ncols, nnz, window_size, graph_layout, itype, vbytes,
+                                 alloc, out, stream);
 }
 
 int spmm_pack_rows_launch(const void *src, const int64_t *inv, int64_t n, int64_t row_bytes, void *dst,

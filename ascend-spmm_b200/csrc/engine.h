@@ -6,9 +6,14 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/spmm_b200.h"
+
 namespace spmmb {
 
 struct DevStatus;
+
+// Records the thread-local error message of the C ABI and returns `code`.
+int capi_error(int code, const char *fmt, ...);
 
 // Per-device sticky status word (status.cu).
 DevStatus *device_status_ptr(cudaError_t *err);
@@ -84,5 +89,17 @@ cudaError_t launch_pack_rows(const void *src, const int64_t *inv, int64_t n, int
                              int64_t packed_rows, DevStatus *st, cudaStream_t stream);
 cudaError_t launch_restore_rows(const void *src, int64_t src_rows, const int64_t *inv, int64_t n,
                                 int64_t row_bytes, void *dst, DevStatus *st, cudaStream_t stream);
+
+// ---- layout builders (preprocess.cu) ----------------------------------------
+
+int pre_csr_to_bcsr(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols, int64_t nnz,
+                    int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc, spmm_layout *out,
+                    void *stream, bool cube);
+int pre_block_level_split(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                          int64_t nnz, double a, int64_t window_size, int itype, int vbytes,
+                          const spmm_allocator *alloc, spmm_layout *out, void *stream);
+int pre_preprocess(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols, int64_t nnz,
+                   int64_t window_size, int graph_layout, int itype, int vbytes, const spmm_allocator *alloc,
+                   spmm_preprocess_result *out, void *stream);
 
 }  // namespace spmmb

@@ -10,6 +10,11 @@
 
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAFunctions.h>
+
+#include <map>
+#include <stdexcept>
+#include <unordered_map>
 
 #include "spmm_b200.h"
 
@@ -239,6 +244,192 @@ at::Tensor spmm_ascend_cube_aiv_mb_impl(MIXED_SIG)
     return mixed_op(MIXED_ARGS, "spmm_ascend_cube_aiv_mb", true, &spmm_ascend_cube_aiv_mb_launch);
 }
 
+// ---------------------------------------------------------------------------
+// Layout builders: csr_to_bcsr, csr_to_ascend_cube, block_level_split,
+// preprocess (custom_op.cpp:429-1412).  Same argument order and dict keys as
+// the reference; inputs may be CPU or CUDA tensors (CPU inputs are copied to
+// the current CUDA device - no CPU compute) and every output lives on that
+// device.  Index outputs keep the input index dtype; permutations and audit
+// counters are int64, costs float64 (custom_op.cpp:1037-1109).
+// ---------------------------------------------------------------------------
+
+// spmm_allocator backed by the torch caching allocator: every block is a
+// uint8 tensor kept alive in `live` until handed out as an output or
+// released as a temporary.
+struct TorchAllocator {
+    at::TensorOptions opts;
+    std::unordered_map<void *, at::Tensor> live;
+    spmm_allocator handle;
+
+    explicit TorchAllocator(const at::Device &dev) : opts(at::TensorOptions().device(dev).dtype(at::kByte))
+    {
+        handle.ctx = this;
+        handle.alloc = &TorchAllocator::alloc;
+        handle.release = &TorchAllocator::release;
+    }
+    static void *alloc(void *ctx, size_t bytes)
+    {
+        auto *self = static_cast<TorchAllocator *>(ctx);
+        try {
+            at::Tensor t = at::empty({(int64_t)bytes}, self->opts);
+            void *p = t.data_ptr();
+            self->live.emplace(p, std::move(t));
+            return p;
+        } catch (...) {
+            return nullptr;
+        }
+    }
+    static void release(void *ctx, void *p) { static_cast<TorchAllocator *>(ctx)->live.erase(p); }
+    at::Tensor take(const spmm_array &a, at::ScalarType st)
+    {
+        if (a.len == 0 || a.data == nullptr) return at::empty({0}, opts.dtype(st));
+        auto it = live.find(a.data);
+        TORCH_CHECK(it != live.end(), "internal: output array not owned by the allocator");
+        at::Tensor raw = it->second;
+        live.erase(it);
+        return raw.narrow(0, 0, a.len * (int64_t)c10::elementSize(st)).view(st);
+    }
+};
+
+struct CsrInput {
+    at::Tensor crow, col, val;
+    int itype;
+    int vbytes;
+};
+
+CsrInput prepare_csr(const at::Tensor &crow_ptr, const at::Tensor &col_indices, const at::Tensor &values,
+                     const char *op)
+{
+    TORCH_CHECK(crow_ptr.dim() == 1 && col_indices.dim() == 1 && values.dim() == 1, op,
+                ": crow_ptr, col_indices and values must be one-dimensional");
+    TORCH_CHECK(crow_ptr.scalar_type() == at::kInt || crow_ptr.scalar_type() == at::kLong, op,
+                ": index tensors must be int32 or int64");
+    TORCH_CHECK(col_indices.scalar_type() == crow_ptr.scalar_type(), op,
+                ": crow_ptr and col_indices must have the same dtype");
+    const at::ScalarType vt = values.scalar_type();
+    TORCH_CHECK(vt == at::kHalf || vt == at::kFloat || vt == at::kDouble, op,
+                ": values must be float16, float32 or float64");
+    TORCH_CHECK(values.size(0) == col_indices.size(0), op, ": col_indices and values must have equal length");
+    TORCH_CHECK(crow_ptr.size(0) >= 1, op, ": crow_ptr must hold nrows + 1 entries");
+    at::Device dev = crow_ptr.is_cuda() ? crow_ptr.device()
+                                        : at::Device(at::kCUDA, c10::cuda::current_device());
+    auto to_dev = [&](const at::Tensor &t) { return t.to(dev).contiguous(); };
+    CsrInput in{to_dev(crow_ptr), to_dev(col_indices), aligned16(to_dev(values)),
+                crow_ptr.scalar_type() == at::kInt ? SPMM_I32 : SPMM_I64, (int)values.element_size()};
+    return in;
+}
+
+void check_rows(const CsrInput &in, int64_t nrows, const char *op)
+{
+    TORCH_CHECK(nrows >= 0 && in.crow.size(0) == nrows + 1, op, ": crow_ptr must hold nrows + 1 = ", nrows + 1,
+                " entries, but has ", in.crow.size(0));
+}
+
+// Layout dict keys of a (window, CSR) pair.
+void put_layout(std::map<std::string, at::Tensor> &d, TorchAllocator &A, const spmm_layout &L, at::ScalarType it,
+                at::ScalarType vt, const std::string &prefix, bool with_v)
+{
+    d[prefix + "crow_window_ptr"] = A.take(L.crow_window_ptr, it);
+    d[prefix + "unique_col_ids"] = A.take(L.unique_col_ids, it);
+    d[prefix + "value"] = A.take(L.value, vt);
+    if (with_v) {
+        d[prefix + "vrow_window_ptr"] = A.take(L.vrow_window_ptr, it);
+        d[prefix + "vcol_indices"] = A.take(L.vcol_indices, it);
+        d[prefix + "vvalue"] = A.take(L.vvalue, vt);
+    }
+}
+
+// Preprocessing errors: occupancy violations raise ValueError like the
+// reference's std::invalid_argument (extension/boundary_bucket_sort.h:34).
+void check_pre(int rc)
+{
+    if (rc == SPMM_OK) return;
+    const std::string msg = spmm_last_error();
+    if (msg.find("block occupancy") != std::string::npos) throw std::invalid_argument(msg);
+    TORCH_CHECK(false, msg);
+}
+
+std::map<std::string, at::Tensor> csr_to_bcsr(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
+                                              int64_t nrows, int64_t ncols, int64_t window_size)
+{
+    CsrInput in = prepare_csr(crow_ptr, col_indices, values, "csr_to_bcsr");
+    check_rows(in, nrows, "csr_to_bcsr");
+    c10::cuda::CUDAGuard guard(in.crow.device());
+    TorchAllocator A(in.crow.device());
+    spmm_layout L{};
+    check_pre(spmm_csr_to_bcsr_run(in.crow.data_ptr(), in.col.data_ptr(), in.val.data_ptr(), nrows, ncols,
+                                   in.col.size(0), window_size, in.itype, in.vbytes, &A.handle, &L, stream_of(in.crow)));
+    std::map<std::string, at::Tensor> d;
+    put_layout(d, A, L, crow_ptr.scalar_type(), values.scalar_type(), "", false);
+    return d;
+}
+
+std::map<std::string, at::Tensor> csr_to_ascend_cube(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
+                                                     int64_t nrows, int64_t ncols, int64_t window_size)
+{
+    CsrInput in = prepare_csr(crow_ptr, col_indices, values, "csr_to_ascend_cube");
+    check_rows(in, nrows, "csr_to_ascend_cube");
+    c10::cuda::CUDAGuard guard(in.crow.device());
+    TorchAllocator A(in.crow.device());
+    spmm_layout L{};
+    check_pre(spmm_csr_to_ascend_cube_run(in.crow.data_ptr(), in.col.data_ptr(), in.val.data_ptr(), nrows, ncols,
+                                          in.col.size(0), window_size, in.itype, in.vbytes, &A.handle, &L,
+                                          stream_of(in.crow)));
+    std::map<std::string, at::Tensor> d;
+    put_layout(d, A, L, crow_ptr.scalar_type(), values.scalar_type(), "", false);
+    return d;
+}
+
+std::map<std::string, at::Tensor> block_level_split(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
+                                                    int64_t nrows, int64_t ncols, double a, int64_t window_size)
+{
+    CsrInput in = prepare_csr(crow_ptr, col_indices, values, "block_level_split");
+    check_rows(in, nrows, "block_level_split");
+    c10::cuda::CUDAGuard guard(in.crow.device());
+    TorchAllocator A(in.crow.device());
+    spmm_layout L{};
+    check_pre(spmm_block_level_split_run(in.crow.data_ptr(), in.col.data_ptr(), in.val.data_ptr(), nrows, ncols,
+                                         in.col.size(0), a, window_size, in.itype, in.vbytes, &A.handle, &L,
+                                         stream_of(in.crow)));
+    std::map<std::string, at::Tensor> d;
+    put_layout(d, A, L, crow_ptr.scalar_type(), values.scalar_type(), "", true);
+    return d;
+}
+
+std::map<std::string, at::Tensor> preprocess(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
+                                             int64_t nrows, int64_t ncols, int64_t window_size, bool graph_layout)
+{
+    CsrInput in = prepare_csr(crow_ptr, col_indices, values, "preprocess");
+    check_rows(in, nrows, "preprocess");
+    c10::cuda::CUDAGuard guard(in.crow.device());
+    TorchAllocator A(in.crow.device());
+    spmm_preprocess_result R{};
+    check_pre(spmm_preprocess_run(in.crow.data_ptr(), in.col.data_ptr(), in.val.data_ptr(), nrows, ncols,
+                                  in.col.size(0), window_size, graph_layout ? 1 : 0, in.itype, in.vbytes, &A.handle,
+                                  &R, stream_of(in.crow)));
+    const at::ScalarType it = crow_ptr.scalar_type(), vt = values.scalar_type();
+    std::map<std::string, at::Tensor> d;
+    put_layout(d, A, R.fwd, it, vt, "", true);
+    d["renumbered_unique_col_ids"] = A.take(R.renumbered_unique_col_ids, it);
+    d["renumbered_vcol_indices"] = A.take(R.renumbered_vcol_indices, it);
+    put_layout(d, A, R.transpose, it, vt, "transpose_", true);
+    d["permutation"] = A.take(R.permutation, at::kLong);
+    d["inv_permutation"] = A.take(R.inv_permutation, at::kLong);
+    auto dev = in.crow.device();
+    auto i64 = [&](int64_t v) { return at::full({1}, v, at::TensorOptions().dtype(at::kLong).device(dev)); };
+    auto f64 = [&](double v) { return at::full({1}, v, at::TensorOptions().dtype(at::kDouble).device(dev)); };
+    d["packed_rows"] = i64(R.packed_rows);
+    d["packed_layout_supported"] = i64(R.packed_layout_supported);
+    d["marginal_window"] = i64(R.marginal_window);
+    d["marginal_aic_blocks"] = i64(R.marginal_aic_blocks);
+    d["marginal_total_blocks"] = i64(R.marginal_total_blocks);
+    d["shared_windows"] = i64(R.shared_windows);
+    d["estimated_aic_cost"] = f64(R.estimated_aic_cost);
+    d["estimated_aiv_cost"] = f64(R.estimated_aiv_cost);
+    d["estimated_max_cost"] = f64(R.estimated_max_cost);
+    return d;
+}
+
 // Row permutation helpers behind pack_node_tensor / restore_node_tensor
 // (spmm_npu.py:22-61); argument checks with the reference's messages stay in
 // the Python wrappers.
@@ -301,6 +492,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m)
           "CSR-path ablation: deeper gather batches (bitwise-identical CSR results)");
     m.def("spmm_csr_aiv_mb_batch", &spmm_csr_aiv_mb_batch_impl,
           "CSR ablation: deeper gather batches (bitwise-identical results)");
+    m.def("csr_to_ascend_cube", &csr_to_ascend_cube,
+          "Convert CSR to the 16 x 16 tile format on the GPU (rows must be sorted). Returns dict with keys "
+          "crow_window_ptr [nwindows + 1], unique_col_ids [total_blocks * 16], value [total_blocks * 256]",
+          pybind11::arg("crow_ptr"), pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"),
+          pybind11::arg("ncols"), pybind11::arg("window_size") = 16);
+    m.def("csr_to_bcsr", &csr_to_bcsr,
+          "Convert CSR to BCSR(16 x 1) on the GPU (rows must be sorted). Returns dict with keys "
+          "crow_window_ptr [nwindows + 1], unique_col_ids [total_blocks], value [total_blocks * 16]",
+          pybind11::arg("crow_ptr"), pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"),
+          pybind11::arg("ncols"), pybind11::arg("window_size") = 16);
+    m.def("preprocess", &preprocess,
+          "Partition coalesced CSR by the calibrated 295/505 GB/s window/CSR bandwidths on the GPU; returns the "
+          "packed window/CSR tensors, row permutations and audit fields (and with graph_layout=True on a square "
+          "graph the P*A*P^T relabel and its fixed-layout transpose), bit-exact with the reference.",
+          pybind11::arg("crow_ptr"), pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"),
+          pybind11::arg("ncols"), pybind11::arg("window_size") = 16, pybind11::arg("graph_layout") = false);
+    m.def("block_level_split", &block_level_split,
+          "Split CSR into (16,1)-BSR + CSR hybrid dict by block density (GPU)", pybind11::arg("crow_ptr"),
+          pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"), pybind11::arg("ncols"),
+          pybind11::arg("a"), pybind11::arg("window_size") = 16);
     m.def("pack_rows", &pack_rows, "dst[index[i]] = src[i]; other rows zero (pack_node_tensor helper)");
     m.def("restore_rows", &restore_rows, "dst[i] = src[index[i]] (restore_node_tensor helper)");
     m.def("device_status", &device_status, "Sticky device-side validation status (code, detail)",

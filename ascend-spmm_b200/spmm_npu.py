@@ -22,15 +22,12 @@ from custom_ops_lib import (  # noqa: F401  (re-exported API)
     spmm_csr_aiv_mb_batch,
 )
 
-try:  # layout functions and the cube-only operator
-    from custom_ops_lib import (  # noqa: F401
-        block_level_split,
-        csr_to_ascend_cube,
-        csr_to_bcsr,
-        preprocess,
-    )
-except ImportError:  # pragma: no cover - only while the module is partially built
-    pass
+from custom_ops_lib import (  # noqa: F401  (GPU layout builders)
+    block_level_split,
+    csr_to_ascend_cube,
+    csr_to_bcsr,
+    preprocess,
+)
 try:
     from custom_ops_lib import spmm_cube  # noqa: F401
 except ImportError:  # pragma: no cover

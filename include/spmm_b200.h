@@ -137,6 +137,70 @@ int spmm_ascend_cube_aiv_mb_launch(
     int dtype, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---------------------------------------------------------------------- */
+/* Layout builders (GPU, bit-exact with the reference's CPU preprocessing). */
+/* Inputs: CSR on the device (crow [nrows + 1], col [nnz], val [nnz] with  */
+/* val element size vbytes = 2, 4 or 8).  Output sizes depend on the data, */
+/* so these calls synchronise `stream`; every output and temporary array is */
+/* obtained from the caller's allocator (outputs stay owned by the caller, */
+/* temporaries are handed back through `release`).  Output index arrays    */
+/* have the input index type; empty arrays have data == NULL, len == 0.    */
+/* ---------------------------------------------------------------------- */
+typedef struct spmm_allocator {
+    void *ctx;
+    void *(*alloc)(void *ctx, size_t bytes);  /* device memory, >= 16-byte aligned; NULL on failure */
+    void (*release)(void *ctx, void *ptr);    /* temporaries; may be NULL */
+} spmm_allocator;
+
+typedef struct spmm_array {
+    void *data;   /* device pointer */
+    int64_t len;  /* elements */
+} spmm_array;
+
+typedef struct spmm_layout {
+    spmm_array crow_window_ptr, unique_col_ids, value;
+    spmm_array vrow_window_ptr, vcol_indices, vvalue;
+} spmm_layout;
+
+typedef struct spmm_preprocess_result {
+    spmm_layout fwd;
+    spmm_layout transpose;                       /* graph layout only */
+    spmm_array renumbered_unique_col_ids;        /* graph layout only */
+    spmm_array renumbered_vcol_indices;          /* graph layout only */
+    spmm_array permutation;                      /* int64 [packed_rows] */
+    spmm_array inv_permutation;                  /* int64 [nrows] */
+    int64_t packed_rows, packed_layout_supported, marginal_window, marginal_aic_blocks,
+        marginal_total_blocks, shared_windows;
+    double estimated_aic_cost, estimated_aiv_cost, estimated_max_cost;
+} spmm_preprocess_result;
+
+/* Replaces csr_to_bcsr / ToBCSR (custom_op.cpp:594-746): per 16-row window,
+ * ascending distinct columns; value[16 b + row].  Rows must be sorted. */
+int spmm_csr_to_bcsr_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                         int64_t nnz, int64_t window_size, int itype, int vbytes,
+                         const spmm_allocator *alloc, spmm_layout *out, void *stream);
+
+/* Replaces csr_to_ascend_cube (custom_op.cpp:429-592): distinct columns in
+ * 16-column tiles (last tile zero-padded); value[256 t + 16 row + k]. */
+int spmm_csr_to_ascend_cube_run(const void *crow, const void *col, const void *val, int64_t nrows,
+                                int64_t ncols, int64_t nnz, int64_t window_size, int itype, int vbytes,
+                                const spmm_allocator *alloc, spmm_layout *out, void *stream);
+
+/* Replaces block_level_split / hybrid_split_impl (custom_op.cpp:1146-1348,
+ * 1390-1412): the k least-dense blocks move to CSR, k = first argmin of
+ * |(#blocks - k) / moved_nnz - a|. */
+int spmm_block_level_split_run(const void *crow, const void *col, const void *val, int64_t nrows,
+                               int64_t ncols, int64_t nnz, double a, int64_t window_size, int itype,
+                               int vbytes, const spmm_allocator *alloc, spmm_layout *out, void *stream);
+
+/* Replaces preprocess / taskmapping (custom_op.cpp:765-1137): calibrated
+ * 295/505 GB/s window split, marginal-window block split, packed row order,
+ * window and CSR packs; with graph_layout on a square matrix also the
+ * P A P^T relabel and its fixed-layout transpose. */
+int spmm_preprocess_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                        int64_t nnz, int64_t window_size, int graph_layout, int itype, int vbytes,
+                        const spmm_allocator *alloc, spmm_preprocess_result *out, void *stream);
+
+/* ---------------------------------------------------------------------- */
 /* Graph-layout row permutation (P and P^T on node tensors).               */
 /* ---------------------------------------------------------------------- */
 
