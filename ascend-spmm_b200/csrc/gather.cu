@@ -147,6 +147,218 @@ csr_gather_kernel(const GatherArgs a)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Stream kernel (rows of >= 16 vectors: N >= 128 fp16, N >= 64 fp32).
+//
+// A group of G lanes (a warp, or a half-warp for G = 16) consumes its unit as
+// one flat nonzero stream instead of row by row: the next 32 column/value
+// entries are prefetched into lanes while the current 32 are gathered, a
+// batch of U gathers per lane is always in flight whatever the row lengths,
+// and row boundaries are handled inline (flush, then advance through the
+// row-pointer cache held in lanes).  The per-row fma order is the same as in
+// csr_gather_kernel, so both produce identical bits.
+// ---------------------------------------------------------------------------
+template <typename I, int G>
+__device__ __forceinline__ int64_t group_lower_bound(const I *a, int64_t L, int64_t H, int64_t key, unsigned gmask,
+                                                     int gl, int shift)
+{
+    while (H - L > G) {
+        const int64_t step = (H - L + G - 1) / G;
+        const int64_t pos = L + (int64_t)gl * step;
+        const bool ge = pos < H && ld_idx(a + pos) >= key;
+        const unsigned m = (__ballot_sync(gmask, ge) & gmask) >> shift;
+        if (m == 0) {
+            const int64_t kmax = min((int64_t)(G - 1), (H - 1 - L) / step);
+            L = L + kmax * step + 1;
+        } else {
+            const int f = __ffs(m) - 1;
+            const int64_t pf = L + (int64_t)f * step;
+            L = (f == 0) ? L : L + (int64_t)(f - 1) * step + 1;
+            H = pf;
+        }
+    }
+    const int64_t pos = L + gl;
+    const bool ge = pos < H && ld_idx(a + pos) >= key;
+    const unsigned m = (__ballot_sync(gmask, ge) & gmask) >> shift;
+    return m ? L + (__ffs(m) - 1) : H;
+}
+
+template <typename T, typename I, int G, int VPL, int U, int MINB>
+__global__ void __launch_bounds__(kGatherThreads, MINB)
+csr_stream_kernel(const GatherArgs a)
+{
+    static_assert(G == 16 || G == 32, "stream groups are half-warps or warps");
+    constexpr int S = 32 / G;
+    constexpr int EPV = Vec<T>::kElems;
+    constexpr int CH = 32;          // nonzeros per prefetched chunk
+    constexpr int PER = CH / G;     // chunk entries held per lane
+    static_assert(CH % U == 0, "batches tile the chunk");
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / G, gl = lane % G, shift = sub * G;
+    const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << shift);
+    const int64_t stream = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * S + sub;
+    const int64_t nstreams = (((int64_t)gridDim.x * blockDim.x) >> 5) * S;
+
+    const I *rowptr = static_cast<const I *>(a.rowptr);
+    const I *col = static_cast<const I *>(a.col);
+    const T *val = static_cast<const T *>(a.val);
+    const uint4 *B = static_cast<const uint4 *>(a.B);
+    uint4 *out = static_cast<uint4 *>(a.out);
+    const int NV = (int)(a.N / EPV);
+
+    for (int64_t u = a.unit_begin + stream; u < a.unit_end; u += nstreams) {
+        const int64_t lo = u * a.unit;
+        const int64_t hi = min(lo + a.unit, a.nnz);
+        const bool last = (u == a.unit_end - 1);
+        const int64_t i0 = group_lower_bound<I, G>(rowptr, a.row_begin, a.M + 1, lo, gmask, gl, shift);
+        int64_t r = i0;
+        if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r = i0 - 1;
+
+        // row-pointer cache: lanes hold rowptr[rc + gl] and rowptr[rc + G + gl]
+        int64_t rc = r;
+        int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
+        int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+        auto rp = [&](int64_t x) -> int64_t {
+            if (x >= rc + 2 * G) {
+                rc = x;
+                rpa = ld_idx(rowptr + min(rc + gl, a.M));
+                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+            } else if (x >= rc + G) {
+                rc += G;
+                rpa = rpb;
+                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+            }
+            return __shfl_sync(gmask, rpa, (int)(x - rc), G);
+        };
+
+        float acc[VPL][EPV];
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+
+        int64_t beg = 0, end = 0, seg_end = 0;
+        bool have_row = false;
+        // Move to the next row with nonzeros in this unit; empty rows owned by
+        // the unit on the way are written as zeros.
+        auto advance = [&]() {
+            have_row = false;
+            for (;;) {
+                ++r;
+                if (r >= a.M) return;
+                beg = rp(r);
+                end = rp(r + 1);
+                if (beg < 0 || end < beg || end > a.nnz) {
+                    if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                    r = a.M;
+                    return;
+                }
+                if (beg >= hi && !last) { r = a.M; return; }
+                if (end > beg) {
+                    have_row = true;
+                    seg_end = min(end, hi);
+                    return;
+                }
+#pragma unroll
+                for (int q = 0; q < VPL; ++q) {
+                    const int vi = gl + q * G;
+                    if (vi < NV) __stcs(out + r * NV + vi, make_uint4(0, 0, 0, 0));
+                }
+            }
+        };
+        r -= 1;
+        advance();
+        if (!have_row) continue;
+        const int64_t s0 = max(lo, beg);
+
+        auto load_chunk = [&](int64_t pos, int *cc, float *vv) {
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int64_t e = pos + gl + k * G;
+                cc[k] = -1;
+                vv[k] = 0.f;
+                if (e < hi) {
+                    const int64_t c = (int64_t)ld_stream(col + e);
+                    if (c >= 0 && c < a.K) {
+                        cc[k] = (int)c;
+                        vv[k] = to_f32(ld_stream(val + e));
+                    } else {
+                        raise_status(a.status, SPMM_DEV_BAD_COLUMN, e);
+                    }
+                }
+            }
+        };
+        int ccur[PER];
+        float vcur[PER];
+        load_chunk(s0, ccur, vcur);
+        for (int64_t pb = s0; pb < hi && have_row; pb += CH) {
+            int cnext[PER];
+            float vnext[PER];
+            load_chunk(pb + CH, cnext, vnext);
+#pragma unroll
+            for (int b = 0; b < CH; b += U) {
+                if (pb + b >= hi) break;
+                uint4 bv[U][VPL];
+                float vj[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int e = b + j;
+                    const int c = __shfl_sync(gmask, ccur[e / G], e % G, G);
+                    vj[j] = __shfl_sync(gmask, vcur[e / G], e % G, G);
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q) {
+                        const int vi = gl + q * G;
+                        bv[j][q] = (c >= 0 && vi < NV) ? __ldg(B + (int64_t)c * NV + vi) : make_uint4(0, 0, 0, 0);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int64_t p = pb + b + j;
+                    if (p >= hi || !have_row) break;
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q) {
+                        float f[EPV];
+                        unpack16<T>(bv[j][q], f);
+#pragma unroll
+                        for (int e = 0; e < EPV; ++e) acc[q][e] = fmaf(vj[j], f[e], acc[q][e]);
+                    }
+                    if (p + 1 == seg_end) {
+                        const bool head = beg < lo, tail = end > hi;
+                        if (!head && !tail) {
+#pragma unroll
+                            for (int q = 0; q < VPL; ++q) {
+                                const int vi = gl + q * G;
+                                if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
+                            }
+                        } else {
+                            float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
+#pragma unroll
+                            for (int q = 0; q < VPL; ++q) {
+                                const int vi = gl + q * G;
+                                if (vi >= NV) continue;
+                                float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                                for (int e = 0; e < EPV; e += 4)
+                                    dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                        advance();
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                ccur[k] = cnext[k];
+                vcur[k] = vnext[k];
+            }
+        }
+    }
+}
+
 // Sums the per-unit partials of every row that crosses a unit boundary, in
 // unit order: tail(u0) + head(u0 + 1) + ... + head(u1).  One warp per unit;
 // a unit owns the fix-up of the split row that starts inside it.
@@ -188,26 +400,36 @@ csr_fixup_kernel(const GatherArgs a)
     }
 }
 
-template <typename T, typename I, int G, int VPL, int U, int MINB>
-cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
+template <typename T, typename I, typename Kern>
+cudaError_t launch_kernel(Kern kern, const GatherArgs &a, int64_t units_per_warp, cudaStream_t stream)
 {
-    auto kern = csr_gather_kernel<T, I, G, VPL, U, MINB>;
     int per_sm = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGatherThreads, 0);
     if (e != cudaSuccess) return e;
-    const int64_t warps_needed = a.unit_end - a.unit_begin;
+    const int64_t units = a.unit_end - a.unit_begin;
+    const int64_t warps_needed = (units + units_per_warp - 1) / units_per_warp;
     int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
     blocks = std::min(blocks, (warps_needed + 7) / 8);
     blocks = std::max<int64_t>(blocks, 1);
     kern<<<(unsigned)blocks, kGatherThreads, 0, stream>>>(a);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (a.unit_end - a.unit_begin > 1) {
-        const int64_t fb = std::min<int64_t>((warps_needed + 7) / 8, 8LL * device_sm_count());
+    if (units > 1) {
+        const int64_t fb = std::min<int64_t>((units + 7) / 8, 8LL * device_sm_count());
         csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
         e = cudaGetLastError();
     }
     return e;
+}
+
+template <typename T, typename I, int G, int VPL, int U, int MINB>
+cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
+{
+    // rows of >= 16 vectors use the flat-stream kernel (identical sums)
+    if constexpr (G >= 16)
+        return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB>, a, 32 / G, stream);
+    else
+        return launch_kernel<T, I>(csr_gather_kernel<T, I, G, VPL, U, MINB>, a, 1, stream);
 }
 
 // U x VPL = 8 sixteen-byte gathers in flight per lane (128 B) at 24 warps/SM
@@ -219,9 +441,9 @@ cudaError_t launch_typed(const GatherArgs &a, int batch_depth, cudaStream_t s)
 {
     const int64_t NV = a.N / Vec<T>::kElems;
     const bool deep = batch_depth != 0;
-#define SPMM_GATHER_CFG(G, VPL, U)                                                        \
-    return deep ? launch_cfg<T, I, G, VPL, 2 * (U), ((VPL) > 1 ? 1 : 2)>(a, s)              \
-                : launch_cfg<T, I, G, VPL, U, ((VPL) > 1 ? 2 : 3)>(a, s)
+#define SPMM_GATHER_CFG(G, VPL, U)                                                         \
+    return deep ? launch_cfg<T, I, G, VPL, 2 * (U), ((G) >= 16 || (VPL) > 1 ? 1 : 2)>(a, s)  \
+                : launch_cfg<T, I, G, VPL, U, ((G) >= 16 || (VPL) > 1 ? 2 : 3)>(a, s)
     if (NV <= 2) SPMM_GATHER_CFG(2, 1, 8);
     if (NV <= 4) SPMM_GATHER_CFG(4, 1, 8);
     if (NV <= 8) SPMM_GATHER_CFG(8, 1, 8);

@@ -57,6 +57,7 @@ def parse_args():
     p.add_argument("--op", choices=("csr", "mixed"), default="csr")
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     return p.parse_args()
 
 
@@ -283,7 +284,44 @@ def run_ours(args, rank, world, local):
     peak, peak_kind = peak_hbm()
     traffic = traffic_per_launch(f"{w.name}:{args.op}", nnz_local)
 
-    # ---- end to end through the public API with host buffers -------------
+    out = {}
+    if not args.no_e2e:
+        out["e2e"] = run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops)
+
+    launches_per_step = 2 if mixed is None else 3
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)" if s == 2 else "f32",
+        "data": "synthetic (seeded generator, BASELINE config shapes)",
+        "config": {"workload": f"{w.name} M=K={w.M} nnz={nnz_global} N={w.N}",
+                   "op": "spmm_csr" if mixed is None else "spmm_ascend_cube(preprocess)",
+                   "parallelism": f"row-shard x{world} (B replicated, C row-sharded)",
+                   "l2": f"inputs larger than L2 (B {B.numel() * B.element_size() / 1e6:.0f} MB), no flush",
+                   "generator": w.params},
+        "gb_per_s": round(bytes_local / (ms_step * 1e-3) / 1e9, 1) if world == 1 else None,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": bytes_local},
+        **out,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(w)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops):
+    """Same SpMM through the public API with HOST inputs: every step copies
+    A (rowptr, col, val) and B from pinned host memory, runs spmm_csr and
+    reads C back into pinned host memory, all inside the timed region."""
+    import spmm_npu
+
+    stream = torch.cuda.current_stream()
+    M_local = rp.numel() - 1
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     h_rp, h_col, h_val, h_B = pin(rp), pin(col), pin(val), pin(B)
     h_out = torch.empty((M_local, w.N), dtype=w.dtype).pin_memory()
@@ -310,32 +348,10 @@ def run_ours(args, rank, world, local):
     e2e_value = flops * args.e2e_steps / (e2e_ms * 1e-3) / 1e9
     h2d = allreduce_sum(float(sum(t.numel() * t.element_size() for t in (h_rp, h_col, h_val, h_B))), world)
     d2h = allreduce_sum(float(h_out.numel() * h_out.element_size()), world)
-    assert torch.equal(h_out.to(dev), step()), "e2e result differs from the resident run"
-
-    launches_per_step = 2 if mixed is None else 3
-    out = {
-        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)" if s == 2 else "f32",
-        "data": "synthetic (seeded generator, BASELINE config shapes)",
-        "config": {"workload": f"{w.name} M=K={w.M} nnz={nnz_global} N={w.N}",
-                   "op": "spmm_csr" if mixed is None else "spmm_ascend_cube(preprocess)",
-                   "parallelism": f"row-shard x{world} (B replicated, C row-sharded)",
-                   "l2": "inputs larger than L2 (B 537 MB), no flush", "generator": w.params},
-        "gb_per_s": round(bytes_local / (ms_step * 1e-3) / 1e9, 1) if world == 1 else None,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": bytes_local},
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
-    }
-
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(w)
-    if rank == 0:
-        print(json.dumps(out), flush=True)
+    ref = spmm_npu.spmm_csr(rp, col, val, B, start)
+    assert torch.equal(h_out.to(dev), ref), "e2e result differs from the resident run"
+    return {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps}
 
 
 def cpu_baseline(w):
