@@ -49,6 +49,23 @@ template <> __device__ __forceinline__ void unpack16<float>(const uint4 &v, floa
     f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
 }
 
+// Same conversion, written as volatile asm so the compiler keeps it at its
+// use site: in loops that revisit the same vectors under different
+// predicates, hoisting the conversion of every vector would multiply the
+// live registers.
+template <typename T> __device__ __forceinline__ void unpack16_at_use(const uint4 &v, float *f);
+template <> __device__ __forceinline__ void unpack16_at_use<__half>(const uint4 &v, float *f)
+{
+    const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        asm volatile("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+                     "cvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+                     : "=f"(f[2 * i]), "=f"(f[2 * i + 1])
+                     : "r"(w[i]));
+}
+template <> __device__ __forceinline__ void unpack16_at_use<float>(const uint4 &v, float *f) { unpack16<float>(v, f); }
+
 // Pack fp32 lanes into a 16-byte vector (round to nearest even for fp16).
 template <typename T> __device__ __forceinline__ uint4 pack16(const float *f);
 template <> __device__ __forceinline__ uint4 pack16<__half>(const float *f)

@@ -28,6 +28,8 @@
 //  * Invalid column indices or row pointers are skipped and reported through
 //    the sticky device status instead of faulting.
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 
 #include "../../include/spmm_b200.h"
 #include "common.cuh"
@@ -295,59 +297,74 @@ csr_stream_kernel(const GatherArgs a)
             int cnext[PER];
             float vnext[PER];
             load_chunk(pb + CH, cnext, vnext);
-#pragma unroll
-            for (int b = 0; b < CH; b += U) {
-                if (pb + b >= hi) break;
+            // Batches are a runtime loop and the row bookkeeping below exists
+            // once, so the kernel stays small in the instruction cache.
+#pragma unroll 1
+            for (int b = 0; b < CH && have_row; b += U) {
+                const int64_t pbase = pb + b;
+                if (pbase >= hi) break;
+                const int nvalid = (int)min((int64_t)U, hi - pbase);
                 uint4 bv[U][VPL];
                 float vj[U];
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
                     const int e = b + j;
-                    const int c = __shfl_sync(gmask, ccur[e / G], e % G, G);
-                    vj[j] = __shfl_sync(gmask, vcur[e / G], e % G, G);
+                    int cw = ccur[0];
+                    float vw = vcur[0];
+#pragma unroll
+                    for (int k = 1; k < PER; ++k)
+                        if (e / G == k) { cw = ccur[k]; vw = vcur[k]; }
+                    const int c = __shfl_sync(gmask, cw, e % G, G);
+                    vj[j] = __shfl_sync(gmask, vw, e % G, G);
 #pragma unroll
                     for (int q = 0; q < VPL; ++q) {
                         const int vi = gl + q * G;
-                        bv[j][q] = (c >= 0 && vi < NV) ? __ldg(B + (int64_t)c * NV + vi) : make_uint4(0, 0, 0, 0);
+                        bv[j][q] = (j < nvalid && c >= 0 && vi < NV) ? __ldg(B + (int64_t)c * NV + vi)
+                                                                      : make_uint4(0, 0, 0, 0);
                     }
                 }
+                // one pass per row that owns positions of this batch
+                int j0 = 0;
+                for (;;) {
+                    const int jend = (int)min((int64_t)nvalid, seg_end - pbase);
 #pragma unroll
-                for (int j = 0; j < U; ++j) {
-                    const int64_t p = pb + b + j;
-                    if (p >= hi || !have_row) break;
+                    for (int j = 0; j < U; ++j) {
+                        if (j < j0 || j >= jend) continue;
 #pragma unroll
-                    for (int q = 0; q < VPL; ++q) {
-                        float f[EPV];
-                        unpack16<T>(bv[j][q], f);
+                        for (int q = 0; q < VPL; ++q) {
+                            float f[EPV];
+                            unpack16_at_use<T>(bv[j][q], f);
 #pragma unroll
-                        for (int e = 0; e < EPV; ++e) acc[q][e] = fmaf(vj[j], f[e], acc[q][e]);
-                    }
-                    if (p + 1 == seg_end) {
-                        const bool head = beg < lo, tail = end > hi;
-                        if (!head && !tail) {
-#pragma unroll
-                            for (int q = 0; q < VPL; ++q) {
-                                const int vi = gl + q * G;
-                                if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
-                            }
-                        } else {
-                            float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
-#pragma unroll
-                            for (int q = 0; q < VPL; ++q) {
-                                const int vi = gl + q * G;
-                                if (vi >= NV) continue;
-                                float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
-#pragma unroll
-                                for (int e = 0; e < EPV; e += 4)
-                                    dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
-                            }
+                            for (int e = 0; e < EPV; ++e) acc[q][e] = fmaf(vj[j], f[e], acc[q][e]);
                         }
-#pragma unroll
-                        for (int q = 0; q < VPL; ++q)
-#pragma unroll
-                            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
-                        advance();
                     }
+                    if (pbase + jend != seg_end) break;   // row continues in the next batch
+                    const bool head = beg < lo, tail = end > hi;
+                    if (!head && !tail) {
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q) {
+                            const int vi = gl + q * G;
+                            if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
+                        }
+                    } else {
+                        float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q) {
+                            const int vi = gl + q * G;
+                            if (vi >= NV) continue;
+                            float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                            for (int e = 0; e < EPV; e += 4)
+                                dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                        for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                    advance();
+                    j0 = jend;
+                    if (!have_row || j0 >= nvalid) break;
                 }
             }
 #pragma unroll
@@ -422,14 +439,27 @@ cudaError_t launch_kernel(Kern kern, const GatherArgs &a, int64_t units_per_warp
     return e;
 }
 
+// Kernel choice for rows of >= 16 vectors: the flat-stream kernel unless the
+// environment variable SPMM_B200_GATHER=row selects the row kernel (both
+// produce identical sums; the knob exists for A/B measurement).
+bool prefer_row_kernel()
+{
+    static const bool row = [] {
+        const char *v = getenv("SPMM_B200_GATHER");
+        return v && strcmp(v, "row") == 0;
+    }();
+    return row;
+}
+
 template <typename T, typename I, int G, int VPL, int U, int MINB>
 cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
 {
-    // rows of >= 16 vectors use the flat-stream kernel (identical sums)
-    if constexpr (G >= 16)
-        return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB>, a, 32 / G, stream);
-    else
-        return launch_kernel<T, I>(csr_gather_kernel<T, I, G, VPL, U, MINB>, a, 1, stream);
+    if constexpr (G >= 16) {
+        if (!prefer_row_kernel())
+            return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB>, a, 32 / G, stream);
+    }
+    return launch_kernel<T, I>(csr_gather_kernel<T, I, G, VPL, U, (G >= 16 && MINB < 3 && VPL == 1) ? MINB + 1 : MINB>,
+                               a, 1, stream);
 }
 
 // U x VPL = 8 sixteen-byte gathers in flight per lane (128 B) at 24 warps/SM
