@@ -100,8 +100,8 @@ static int check_csr(int64_t nrows, int64_t ncols, int64_t nnz,
 /* ------------------------------------------------------------------------ */
 /* 16-way window merge shared by csr_to_bcsr and csr_to_ascend_cube.        */
 /*                                                                          */
-/* Follows the merge loop of ToBCSR (extension/custom_op.cpp:611-701) and   */
-/* of the tile converter (custom_op.cpp:479-543): each row of the window    */
+/* Follows the merge loop of ToBCSR (extension/custom_op.cpp:611-671) and   */
+/* of the tile converter (custom_op.cpp:446-519): each row of the window    */
 /* keeps a cursor; every step takes the smallest current column, the lowest */
 /* row winning ties (std::min_element semantics), and emits (row, p).  An   */
 /* exhausted row drops out.  The reference reads col[] one past an          */
@@ -143,7 +143,7 @@ static void bcsr_emit(void *vctx, int64_t i, int64_t c, int64_t p)
 {
     bcsr_ctx *x = (bcsr_ctx *)vctx;
     if (c != x->last) { x->uniq[x->n_uniq++] = c; x->last = c; }
-    /* value[16 * block + row], custom_op.cpp:687 (stride is always 16) */
+    /* value[16 * block + row], custom_op.cpp:661 (stride is always 16) */
     memcpy(x->value + (16 * (x->n_uniq - 1) + i) * x->esz, x->val + p * x->esz, (size_t)x->esz);
 }
 
@@ -183,7 +183,7 @@ static void cube_emit(void *vctx, int64_t i, int64_t c, int64_t p)
         if (++x->cnt == 16) { x->cnt = 0; ++x->n_tile; }
         x->last = c;
     }
-    /* value[256 * tile + 16 * row + k], custom_op.cpp:528 */
+    /* value[256 * tile + 16 * row + k], custom_op.cpp:501 */
     memcpy(x->value + (256 * x->n_tile + 16 * i + x->cnt) * x->esz, x->val + p * x->esz,
            (size_t)x->esz);
 }
