@@ -94,6 +94,22 @@ int spmm_csr_aiv_mb_batch_launch(const void *rowptr, const void *col, const void
                                  int itype, int dtype, void *workspace,
                                  size_t workspace_bytes, void *stream);
 
+/* CSR SpMM for callers that cannot allocate device memory when they call
+ * (for example a service binding this ABI through cgo/JNI/FFI with a device
+ * memory budget fixed at start-up, or a latency-critical loop where a
+ * cudaMalloc would synchronise the device).  No counterpart in the
+ * reference: it is spmm_csr_launch without the workspace argument.  Its
+ * scratch (fp32 partial rows) lives in a 32 MiB static device array that
+ * every GPU loading this library keeps until the process exits; it
+ * allocates nothing, neither by CUDA nor by any library.  The first call on
+ * a device looks the array up with cudaGetSymbolAddress, so make that first
+ * call before any stream capture.  Problems whose partial rows do not fit
+ * even with coarser work units return SPMM_ERR_UNSUPPORTED.  All calls share
+ * the array: calls that overlap on the GPU (other streams or threads) race. */
+int spmm_csr_launch_noalloc(const void *rowptr, const void *col, const void *value, const void *dense,
+                            void *out, int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype,
+                            void *stream);
+
 /* ---------------------------------------------------------------------- */
 /* Mixed window/CSR SpMM.  Output rows = max(16 * n_windows, v_rows)       */
 /* (custom_op.cpp:146).  Window slot s adds its (16 x 1)-block products to  */
