@@ -58,6 +58,8 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    p.add_argument("--gather", action="store_true",
+                   help="also time the optional NCCL all-gather of the row-sharded C (reported separately)")
     return p.parse_args()
 
 
@@ -105,23 +107,6 @@ def allreduce_sum(x: float, world) -> float:
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.SUM)
     return float(t.item())
-
-
-def shard_bounds(rowptr: torch.Tensor, world: int, rank: int):
-    """Rows [r0, r1) of this rank: cut points balance nonzeros and fall on
-    16-row window boundaries."""
-    M = rowptr.numel() - 1
-    if world == 1:
-        return 0, M
-    win = rowptr[::16].to(torch.int64)
-    if win[-1].item() != rowptr[-1].item():
-        win = torch.cat([win, rowptr[-1:].to(torch.int64)])
-    nnz = int(rowptr[-1])
-    targets = torch.tensor([k * nnz // world for k in range(world + 1)], dtype=torch.int64, device=win.device)
-    cut = torch.searchsorted(win, targets).clamp(max=win.numel() - 1) * 16
-    cut = cut.clamp(max=M)
-    cut[0], cut[-1] = 0, M
-    return int(cut[rank]), int(cut[rank + 1])
 
 
 # --------------------------------------------------------------------------
@@ -235,7 +220,10 @@ def run_ours(args, rank, world, local):
     dev = torch.device("cuda", local)
     w = workloads.make(args.config, device=dev, scale=args.scale)
     nnz_global = w.nnz
-    r0, r1 = shard_bounds(w.rowptr, world, rank)
+    from spmm_dist import allgather_rows, shard_bounds
+
+    bounds = shard_bounds(w.rowptr, world)
+    r0, r1 = bounds[rank]
     rp, col, val = workloads.row_slice(w, r0, r1)
     rp, col, val = rp.contiguous(), col.contiguous(), val.contiguous()
     B = w.B
@@ -285,6 +273,20 @@ def run_ours(args, rank, world, local):
     traffic = traffic_per_launch(f"{w.name}:{args.op}", nnz_local)
 
     out = {}
+    if args.gather and world > 1:
+        y = step()
+        allgather_rows(y, bounds)
+        torch.cuda.synchronize()
+        barrier(world)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(5):
+            full = allgather_rows(y, bounds)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gms = allreduce_max(g0.elapsed_time(g1), world) / 5
+        out["allgather"] = {"ms": round(gms, 3), "bytes": int(full.numel() * full.element_size()),
+                            "note": "optional full-C all-gather over NCCL, not part of value"}
     if not args.no_e2e:
         out["e2e"] = run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops)
 

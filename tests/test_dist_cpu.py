@@ -1,0 +1,83 @@
+"""Multi-rank host logic on CPU (gloo, world_size 2): row partition, shard
+slicing and the all-gather of row-sharded C.  The per-rank product is the
+float64 oracle here (no GPU); the GPU path is the same code with
+spmm_npu.spmm_csr as the local operator."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle
+import workloads
+from spmm_dist import allgather_rows, shard_bounds, shard_csr
+
+
+def test_shard_bounds_balanced_and_window_aligned():
+    w = workloads.make(2, scale=0.02)
+    for world in (1, 2, 3, 4, 8):
+        b = shard_bounds(w.rowptr, world)
+        assert len(b) == world and b[0][0] == 0 and b[-1][1] == w.M
+        for (a0, a1), (c0, c1) in zip(b, b[1:]):
+            assert a1 == c0
+        for r0, r1 in b:
+            assert r0 % 16 == 0 and r0 <= r1
+        nz = [int(w.rowptr[r1]) - int(w.rowptr[r0]) for r0, r1 in b]
+        assert sum(nz) == w.nnz
+        # balance within one window's worth of nonzeros plus the largest row
+        deg = (w.rowptr[1:] - w.rowptr[:-1]).to(torch.int64)
+        slack = int(deg.max()) * 16
+        assert max(nz) - w.nnz / world <= slack
+
+
+def test_shard_bounds_degenerate():
+    rp = torch.tensor([0, 2, 2, 5], dtype=torch.int32)
+    assert shard_bounds(rp, 4) == [(0, 3), (3, 3), (3, 3), (3, 3)]
+    assert shard_bounds(torch.zeros(1, dtype=torch.int32), 2) == [(0, 0), (0, 0)]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = workloads.make(3, scale=0.01)
+        bounds = shard_bounds(w.rowptr, world)
+        r0, r1 = bounds[rank]
+        rp, c, v = shard_csr(w.rowptr, w.col, w.val, r0, r1)
+        local = torch.from_numpy(oracle.spmm_csr_f64(rp, c, v, w.B))
+        full = allgather_rows(local, bounds)
+        results[rank] = full.numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allgather_reassembles_full_product():
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        w = workloads.make(3, scale=0.01)
+        ref = oracle.spmm_csr_f64(w.rowptr, w.col, w.val, w.B)
+        for r in range(world):
+            np.testing.assert_allclose(results[r], ref, rtol=0, atol=0)
