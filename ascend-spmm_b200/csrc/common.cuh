@@ -66,6 +66,45 @@ template <> __device__ __forceinline__ void unpack16_at_use<__half>(const uint4 
 }
 template <> __device__ __forceinline__ void unpack16_at_use<float>(const uint4 &v, float *f) { unpack16<float>(v, f); }
 
+// acc[e] += v * b[e] over one 16-byte vector of B, fp32 accumulation.
+// fp16: fma.rn.f32.f16 takes the fp16 operands directly; both are exact in
+// fp32 and so is their product, so each step rounds once, bit-identical to
+// fmaf((float)v, (float)b[e], acc[e]) without separate conversions.
+// fp32: two packed fma.rn.f32x2 (each lane an IEEE fp32 fma).
+template <typename T> struct FmaVec;
+template <> struct FmaVec<__half> {
+    using Scalar = unsigned short;   // fp16 bits of the nonzero's value
+    static __device__ __forceinline__ void run(float *acc, Scalar v, const uint4 &b)
+    {
+        const unsigned w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            asm("{\n\t.reg .f16 s, l, u;\n\tmov.b16 s, %2;\n\tmov.b32 {l, u}, %3;\n\t"
+                "fma.rn.f32.f16 %0, s, l, %0;\n\tfma.rn.f32.f16 %1, s, u, %1;\n\t}"
+                : "+f"(acc[2 * i]), "+f"(acc[2 * i + 1])
+                : "h"(v), "r"(w[i]));
+    }
+    static __device__ __forceinline__ Scalar load(const __half *p)
+    {
+        return __ldcs(reinterpret_cast<const unsigned short *>(p));
+    }
+    static __device__ __forceinline__ Scalar zero() { return 0; }
+};
+template <> struct FmaVec<float> {
+    using Scalar = float;
+    static __device__ __forceinline__ void run(float *acc, Scalar v, const uint4 &b)
+    {
+        asm("{\n\t.reg .b64 a, x, vv;\n\tmov.b64 vv, {%4, %4};\n\t"
+            "mov.b64 a, {%0, %1};\n\tmov.b64 x, {%5, %6};\n\tfma.rn.f32x2 a, vv, x, a;\n\tmov.b64 {%0, %1}, a;\n\t"
+            "mov.b64 a, {%2, %3};\n\tmov.b64 x, {%7, %8};\n\tfma.rn.f32x2 a, vv, x, a;\n\tmov.b64 {%2, %3}, a;\n\t}"
+            : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3])
+            : "f"(v), "f"(__uint_as_float(b.x)), "f"(__uint_as_float(b.y)), "f"(__uint_as_float(b.z)),
+              "f"(__uint_as_float(b.w)));
+    }
+    static __device__ __forceinline__ Scalar load(const float *p) { return __ldcs(p); }
+    static __device__ __forceinline__ Scalar zero() { return 0.f; }
+};
+
 // Pack fp32 lanes into a 16-byte vector (round to nearest even for fp16).
 template <typename T> __device__ __forceinline__ uint4 pack16(const float *f);
 template <> __device__ __forceinline__ uint4 pack16<__half>(const float *f)

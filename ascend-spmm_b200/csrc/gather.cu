@@ -190,11 +190,13 @@ __global__ void __launch_bounds__(kGatherThreads, MINB)
 csr_stream_kernel(const GatherArgs a)
 {
     static_assert(G == 16 || G == 32, "stream groups are half-warps or warps");
+    using F = FmaVec<T>;
+    using Scalar = typename F::Scalar;
     constexpr int S = 32 / G;
     constexpr int EPV = Vec<T>::kElems;
     constexpr int CH = 32;          // nonzeros per prefetched chunk
     constexpr int PER = CH / G;     // chunk entries held per lane
-    static_assert(CH % U == 0, "batches tile the chunk");
+    static_assert(CH % U == 0 && U <= 32, "batches tile the chunk");
     const int lane = threadIdx.x & 31;
     const int sub = lane / G, gl = lane % G, shift = sub * G;
     const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << shift);
@@ -216,12 +218,14 @@ csr_stream_kernel(const GatherArgs a)
         int64_t r = i0;
         if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r = i0 - 1;
 
-        // row-pointer cache: lanes hold rowptr[rc + gl] and rowptr[rc + G + gl]
+        // Row-pointer cache: lanes hold rowptr[rc + gl] and rowptr[rc + G + gl].
+        // rp(x) follows the current row (x never decreases) and slides the
+        // window; rp_peek(x) looks ahead without moving it.
         int64_t rc = r;
         int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
         int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
         auto rp = [&](int64_t x) -> int64_t {
-            if (x >= rc + 2 * G) {
+            if (x < rc || x >= rc + 2 * G) {
                 rc = x;
                 rpa = ld_idx(rowptr + min(rc + gl, a.M));
                 rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
@@ -232,6 +236,13 @@ csr_stream_kernel(const GatherArgs a)
             }
             return __shfl_sync(gmask, rpa, (int)(x - rc), G);
         };
+        auto rp_peek = [&](int64_t x) -> int64_t {
+            if (x >= rc && x < rc + 2 * G) {
+                const int64_t w = (x - rc < G) ? rpa : rpb;
+                return __shfl_sync(gmask, w, (int)((x - rc) & (G - 1)), G);
+            }
+            return ld_idx(rowptr + min(x, a.M));
+        };
 
         float acc[VPL][EPV];
 #pragma unroll
@@ -239,14 +250,13 @@ csr_stream_kernel(const GatherArgs a)
 #pragma unroll
             for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
 
-        int64_t beg = 0, end = 0, seg_end = 0;
+        int64_t beg = 0, end = 0;
         bool have_row = false;
-        // Move to the next row with nonzeros in this unit; empty rows owned by
-        // the unit on the way are written as zeros.
-        auto advance = [&]() {
+        // Make row r (or the next one) current: empty rows owned by this unit
+        // are written as zeros; stops at the first row with nonzeros.
+        auto settle = [&]() {
             have_row = false;
             for (;;) {
-                ++r;
                 if (r >= a.M) return;
                 beg = rp(r);
                 end = rp(r + 1);
@@ -256,34 +266,58 @@ csr_stream_kernel(const GatherArgs a)
                     return;
                 }
                 if (beg >= hi && !last) { r = a.M; return; }
-                if (end > beg) {
-                    have_row = true;
-                    seg_end = min(end, hi);
-                    return;
-                }
+                if (end > beg) { have_row = true; return; }
 #pragma unroll
                 for (int q = 0; q < VPL; ++q) {
                     const int vi = gl + q * G;
                     if (vi < NV) __stcs(out + r * NV + vi, make_uint4(0, 0, 0, 0));
                 }
+                ++r;
             }
         };
-        r -= 1;
-        advance();
+        // Store the finished (segment of the) current row, move to the next.
+        auto flush = [&]() {
+            const bool head = beg < lo, tail = end > hi;
+            if (!head && !tail) {
+#pragma unroll
+                for (int q = 0; q < VPL; ++q) {
+                    const int vi = gl + q * G;
+                    if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
+                }
+            } else {
+                float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
+#pragma unroll
+                for (int q = 0; q < VPL; ++q) {
+                    const int vi = gl + q * G;
+                    if (vi >= NV) continue;
+                    float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                    for (int e = 0; e < EPV; e += 4)
+                        dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+            ++r;
+            settle();
+        };
+        settle();
         if (!have_row) continue;
         const int64_t s0 = max(lo, beg);
 
-        auto load_chunk = [&](int64_t pos, int *cc, float *vv) {
+        auto load_chunk = [&](int64_t pos, int *cc, Scalar *vv) {
 #pragma unroll
             for (int k = 0; k < PER; ++k) {
                 const int64_t e = pos + gl + k * G;
                 cc[k] = -1;
-                vv[k] = 0.f;
+                vv[k] = F::zero();
                 if (e < hi) {
                     const int64_t c = (int64_t)ld_stream(col + e);
                     if (c >= 0 && c < a.K) {
                         cc[k] = (int)c;
-                        vv[k] = to_f32(ld_stream(val + e));
+                        vv[k] = F::load(val + e);
                     } else {
                         raise_status(a.status, SPMM_DEV_BAD_COLUMN, e);
                     }
@@ -291,26 +325,24 @@ csr_stream_kernel(const GatherArgs a)
             }
         };
         int ccur[PER];
-        float vcur[PER];
+        Scalar vcur[PER];
         load_chunk(s0, ccur, vcur);
         for (int64_t pb = s0; pb < hi && have_row; pb += CH) {
             int cnext[PER];
-            float vnext[PER];
+            Scalar vnext[PER];
             load_chunk(pb + CH, cnext, vnext);
-            // Batches are a runtime loop and the row bookkeeping below exists
-            // once, so the kernel stays small in the instruction cache.
 #pragma unroll 1
             for (int b = 0; b < CH && have_row; b += U) {
                 const int64_t pbase = pb + b;
                 if (pbase >= hi) break;
                 const int nvalid = (int)min((int64_t)U, hi - pbase);
                 uint4 bv[U][VPL];
-                float vj[U];
+                Scalar vj[U];
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
                     const int e = b + j;
                     int cw = ccur[0];
-                    float vw = vcur[0];
+                    Scalar vw = vcur[0];
 #pragma unroll
                     for (int k = 1; k < PER; ++k)
                         if (e / G == k) { cw = ccur[k]; vw = vcur[k]; }
@@ -323,48 +355,21 @@ csr_stream_kernel(const GatherArgs a)
                                                                       : make_uint4(0, 0, 0, 0);
                     }
                 }
-                // one pass per row that owns positions of this batch
-                int j0 = 0;
-                for (;;) {
-                    const int jend = (int)min((int64_t)nvalid, seg_end - pbase);
+                // Bit j set: a row's segment ends at position pbase + j (rows
+                // ending in this batch, plus the unit's last position).
+                unsigned ends = (pbase + nvalid == hi) ? (1u << (nvalid - 1)) : 0u;
+                for (int64_t x = r + 1; x <= a.M; ++x) {
+                    const int64_t e = rp_peek(x);
+                    if (e > pbase + nvalid) break;
+                    if (e > pbase) ends |= 1u << (int)(e - pbase - 1);
+                }
 #pragma unroll
-                    for (int j = 0; j < U; ++j) {
-                        if (j < j0 || j >= jend) continue;
+                for (int j = 0; j < U; ++j) {
+                    if (j < nvalid) {
 #pragma unroll
-                        for (int q = 0; q < VPL; ++q) {
-                            float f[EPV];
-                            unpack16_at_use<T>(bv[j][q], f);
-#pragma unroll
-                            for (int e = 0; e < EPV; ++e) acc[q][e] = fmaf(vj[j], f[e], acc[q][e]);
-                        }
+                        for (int q = 0; q < VPL; ++q) F::run(acc[q], vj[j], bv[j][q]);
                     }
-                    if (pbase + jend != seg_end) break;   // row continues in the next batch
-                    const bool head = beg < lo, tail = end > hi;
-                    if (!head && !tail) {
-#pragma unroll
-                        for (int q = 0; q < VPL; ++q) {
-                            const int vi = gl + q * G;
-                            if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
-                        }
-                    } else {
-                        float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
-#pragma unroll
-                        for (int q = 0; q < VPL; ++q) {
-                            const int vi = gl + q * G;
-                            if (vi >= NV) continue;
-                            float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
-#pragma unroll
-                            for (int e = 0; e < EPV; e += 4)
-                                dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
-                        }
-                    }
-#pragma unroll
-                    for (int q = 0; q < VPL; ++q)
-#pragma unroll
-                        for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
-                    advance();
-                    j0 = jend;
-                    if (!have_row || j0 >= nvalid) break;
+                    if ((ends >> j) & 1u) flush();
                 }
             }
 #pragma unroll

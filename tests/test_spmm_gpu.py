@@ -262,3 +262,48 @@ def test_pack_restore_roundtrip(npu):
         npu.pack_node_tensor(torch.zeros(n, 2, device=DEV), inv.to(DEV), 10)
     with pytest.raises(ValueError, match="one entry per original node"):
         npu.pack_node_tensor(torch.zeros(n + 1, 2, device=DEV), inv.to(DEV))
+
+
+_ROW_KERNEL_SNIPPET = r"""
+import sys, torch
+sys.path[:0] = sys.argv[3].split(":")
+import spmm_npu
+d = torch.load(sys.argv[1])
+outs = []
+for case in d:
+    crow, col, val, B = (t.cuda() for t in case)
+    s = torch.zeros(40, dtype=torch.int32, device="cuda")
+    outs.append(spmm_npu.spmm_csr(crow, col, val, B, s).cpu())
+torch.save(outs, sys.argv[2])
+"""
+
+
+def test_stream_and_row_kernels_bitwise_identical(npu, tmp_path):
+    """The flat-stream kernel (mixed-precision fma.rn.f32.f16 / packed f32x2
+    fma) and the row kernel (convert + fmaf) produce the same bits for every
+    width and index type; the row kernel runs in a child process selected by
+    SPMM_B200_GATHER=row."""
+    import os
+    import subprocess
+    import sys
+
+    cases = []
+    for N, dtype, idt in [(128, torch.float16, torch.int32), (256, torch.float16, torch.int64),
+                          (512, torch.float16, torch.int32), (1024, torch.float16, torch.int32),
+                          (64, torch.float32, torch.int32), (512, torch.float32, torch.int64)]:
+        crow, col = rand_csr(1500, 900, 0.02, seed=N, long_rows={3: 700, 1499: 880}, empty_every=11, idt=idt)
+        g = torch.Generator().manual_seed(N)
+        val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
+        B = torch.randn(900, N, generator=g).to(dtype)
+        cases.append((crow, col, val, B))
+    ours = [csr_call(npu, *c).cpu() for c in cases]
+    src, dst = tmp_path / "in.pt", tmp_path / "out.pt"
+    torch.save(cases, src)
+    here = os.path.dirname(os.path.abspath(__file__))
+    paths = ":".join([os.path.join(here, "..", "ascend-spmm_b200"), here])
+    env = dict(os.environ, SPMM_B200_GATHER="row")
+    subprocess.run([sys.executable, "-c", _ROW_KERNEL_SNIPPET, str(src), str(dst), paths], env=env, check=True,
+                   timeout=300)
+    theirs = torch.load(dst)
+    for (c, a, b) in zip(cases, ours, theirs):
+        assert torch.equal(a, b), (c[3].shape, c[3].dtype)
