@@ -218,9 +218,9 @@ csr_stream_kernel(const GatherArgs a)
         int64_t r = i0;
         if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r = i0 - 1;
 
-        // Row-pointer cache: lanes hold rowptr[rc + gl] and rowptr[rc + G + gl].
+        // Row-pointer cache: lanes hold rowptr[rc + gl] and rowptr[rc + G + gl];
         // rp(x) follows the current row (x never decreases) and slides the
-        // window; rp_peek(x) looks ahead without moving it.
+        // window forward.
         int64_t rc = r;
         int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
         int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
@@ -236,13 +236,6 @@ csr_stream_kernel(const GatherArgs a)
             }
             return __shfl_sync(gmask, rpa, (int)(x - rc), G);
         };
-        auto rp_peek = [&](int64_t x) -> int64_t {
-            if (x >= rc && x < rc + 2 * G) {
-                const int64_t w = (x - rc < G) ? rpa : rpb;
-                return __shfl_sync(gmask, w, (int)((x - rc) & (G - 1)), G);
-            }
-            return ld_idx(rowptr + min(x, a.M));
-        };
 
         float acc[VPL][EPV];
 #pragma unroll
@@ -250,62 +243,31 @@ csr_stream_kernel(const GatherArgs a)
 #pragma unroll
             for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
 
+        // Current row: r with [beg, end); rows before it are finished.
+        // Empty rows owned by this unit are written as zeros on the way.
         int64_t beg = 0, end = 0;
         bool have_row = false;
-        // Make row r (or the next one) current: empty rows owned by this unit
-        // are written as zeros; stops at the first row with nonzeros.
-        auto settle = [&]() {
-            have_row = false;
-            for (;;) {
-                if (r >= a.M) return;
-                beg = rp(r);
-                end = rp(r + 1);
-                if (beg < 0 || end < beg || end > a.nnz) {
-                    if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
-                    r = a.M;
-                    return;
-                }
-                if (beg >= hi && !last) { r = a.M; return; }
-                if (end > beg) { have_row = true; return; }
+        auto zero_row = [&](int64_t row) {
 #pragma unroll
-                for (int q = 0; q < VPL; ++q) {
-                    const int vi = gl + q * G;
-                    if (vi < NV) __stcs(out + r * NV + vi, make_uint4(0, 0, 0, 0));
-                }
-                ++r;
+            for (int q = 0; q < VPL; ++q) {
+                const int vi = gl + q * G;
+                if (vi < NV) __stcs(out + row * NV + vi, make_uint4(0, 0, 0, 0));
             }
         };
-        // Store the finished (segment of the) current row, move to the next.
-        auto flush = [&]() {
-            const bool head = beg < lo, tail = end > hi;
-            if (!head && !tail) {
-#pragma unroll
-                for (int q = 0; q < VPL; ++q) {
-                    const int vi = gl + q * G;
-                    if (vi < NV) __stcs(out + r * NV + vi, pack16<T>(acc[q]));
-                }
-            } else {
-                float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
-#pragma unroll
-                for (int q = 0; q < VPL; ++q) {
-                    const int vi = gl + q * G;
-                    if (vi >= NV) continue;
-                    float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
-#pragma unroll
-                    for (int e = 0; e < EPV; e += 4)
-                        dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
-                }
+        for (; r < a.M; ++r) {
+            beg = rp(r);
+            end = rp(r + 1);
+            if (beg < 0 || end < beg || end > a.nnz) {
+                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                break;
             }
-#pragma unroll
-            for (int q = 0; q < VPL; ++q)
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
-            ++r;
-            settle();
-        };
-        settle();
+            if (beg >= hi && !last) break;
+            if (end > beg) { have_row = true; break; }
+            zero_row(r);
+        }
         if (!have_row) continue;
         const int64_t s0 = max(lo, beg);
+        bool head_pending = beg < lo;   // the first segment is a head partial
 
         auto load_chunk = [&](int64_t pos, int *cc, Scalar *vv) {
 #pragma unroll
@@ -324,15 +286,31 @@ csr_stream_kernel(const GatherArgs a)
                 }
             }
         };
+        // fp32 partial row of this unit: slot 0 = head (row began before lo),
+        // slot 1 = tail (row continues past hi).
+        auto store_partial = [&](int slot) {
+            float *prow = a.partial + ((u - a.unit_begin) * 2 + slot) * a.N;
+#pragma unroll
+            for (int q = 0; q < VPL; ++q) {
+                const int vi = gl + q * G;
+                if (vi >= NV) continue;
+                float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                for (int e = 0; e < EPV; e += 4)
+                    dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+            }
+        };
+
         int ccur[PER];
         Scalar vcur[PER];
         load_chunk(s0, ccur, vcur);
-        for (int64_t pb = s0; pb < hi && have_row; pb += CH) {
+        bool done = false;
+        for (int64_t pb = s0; pb < hi && !done; pb += CH) {
             int cnext[PER];
             Scalar vnext[PER];
             load_chunk(pb + CH, cnext, vnext);
 #pragma unroll 1
-            for (int b = 0; b < CH && have_row; b += U) {
+            for (int b = 0; b < CH && !done; b += U) {
                 const int64_t pbase = pb + b;
                 if (pbase >= hi) break;
                 const int nvalid = (int)min((int64_t)U, hi - pbase);
@@ -355,13 +333,41 @@ csr_stream_kernel(const GatherArgs a)
                                                                       : make_uint4(0, 0, 0, 0);
                     }
                 }
-                // Bit j set: a row's segment ends at position pbase + j (rows
-                // ending in this batch, plus the unit's last position).
-                unsigned ends = (pbase + nvalid == hi) ? (1u << (nvalid - 1)) : 0u;
-                for (int64_t x = r + 1; x <= a.M; ++x) {
-                    const int64_t e = rp_peek(x);
-                    if (e > pbase + nvalid) break;
-                    if (e > pbase) ends |= 1u << (int)(e - pbase - 1);
+                // Row bookkeeping for the batch, done once while the gathers
+                // are in flight: bit j of `ends` is set when a row segment
+                // ends at position pbase + j, and lane j then holds that row;
+                // `tails` marks a segment cut by the unit's end.
+                unsigned ends = 0, tails = 0;
+                int64_t myrow = 0;
+                const int64_t bend = pbase + nvalid;
+                for (;;) {
+                    if (end <= bend) {                      // row r ends in this batch
+                        const int jb = (int)(end - pbase - 1);
+                        ends |= 1u << jb;
+                        if (gl == jb) myrow = r;
+                        int64_t prev = end;
+                        bool next = false;
+                        for (++r; r < a.M; ++r) {
+                            beg = prev;
+                            end = rp(r + 1);
+                            if (end < beg || end > a.nnz) {
+                                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                                break;
+                            }
+                            if (beg >= hi && !last) break;
+                            if (end > beg) { next = true; break; }
+                            zero_row(r);
+                        }
+                        if (!next) { done = true; break; }
+                        continue;
+                    }
+                    if (bend == hi) {                       // row r continues past the unit
+                        ends |= 1u << (nvalid - 1);
+                        tails |= 1u << (nvalid - 1);
+                        if (gl == nvalid - 1) myrow = r;
+                        done = true;
+                    }
+                    break;
                 }
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
@@ -369,7 +375,23 @@ csr_stream_kernel(const GatherArgs a)
 #pragma unroll
                         for (int q = 0; q < VPL; ++q) F::run(acc[q], vj[j], bv[j][q]);
                     }
-                    if ((ends >> j) & 1u) flush();
+                    if ((ends >> j) & 1u) {
+                        if (head_pending || ((tails >> j) & 1u)) {
+                            store_partial(head_pending ? 0 : 1);
+                            head_pending = false;
+                        } else {
+                            const int64_t row = __shfl_sync(gmask, myrow, j, G);
+#pragma unroll
+                            for (int q = 0; q < VPL; ++q) {
+                                const int vi = gl + q * G;
+                                if (vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                    }
                 }
             }
 #pragma unroll
