@@ -185,7 +185,8 @@ __device__ __forceinline__ int64_t group_lower_bound(const I *a, int64_t L, int6
     return m ? L + (__ffs(m) - 1) : H;
 }
 
-template <typename T, typename I, int G, int VPL, int U, int MINB>
+// FULL: every lane owns VPL valid vectors (N * sizeof(T) / 16 == G * VPL).
+template <typename T, typename I, int G, int VPL, int U, int MINB, bool FULL>
 __global__ void __launch_bounds__(kGatherThreads, MINB)
 csr_stream_kernel(const GatherArgs a)
 {
@@ -209,6 +210,7 @@ csr_stream_kernel(const GatherArgs a)
     const uint4 *B = static_cast<const uint4 *>(a.B);
     uint4 *out = static_cast<uint4 *>(a.out);
     const int NV = (int)(a.N / EPV);
+    const uint4 *Bl = B + gl;
 
     for (int64_t u = a.unit_begin + stream; u < a.unit_end; u += nstreams) {
         const int64_t lo = u * a.unit;
@@ -269,11 +271,13 @@ csr_stream_kernel(const GatherArgs a)
         const int64_t s0 = max(lo, beg);
         bool head_pending = beg < lo;   // the first segment is a head partial
 
+        // Invalid columns become column 0 with value 0 (this kernel runs only
+        // with K > 0), so the gather needs no predicate beyond the batch end.
         auto load_chunk = [&](int64_t pos, int *cc, Scalar *vv) {
 #pragma unroll
             for (int k = 0; k < PER; ++k) {
                 const int64_t e = pos + gl + k * G;
-                cc[k] = -1;
+                cc[k] = 0;
                 vv[k] = F::zero();
                 if (e < hi) {
                     const int64_t c = (int64_t)ld_stream(col + e);
@@ -326,11 +330,11 @@ csr_stream_kernel(const GatherArgs a)
                         if (e / G == k) { cw = ccur[k]; vw = vcur[k]; }
                     const int c = __shfl_sync(gmask, cw, e % G, G);
                     vj[j] = __shfl_sync(gmask, vw, e % G, G);
+                    if (j < nvalid) {
+                        const uint4 *brow = Bl + (int64_t)c * NV;
 #pragma unroll
-                    for (int q = 0; q < VPL; ++q) {
-                        const int vi = gl + q * G;
-                        bv[j][q] = (j < nvalid && c >= 0 && vi < NV) ? __ldg(B + (int64_t)c * NV + vi)
-                                                                      : make_uint4(0, 0, 0, 0);
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV) bv[j][q] = __ldg(brow + q * G);
                     }
                 }
                 // Row bookkeeping for the batch, done once while the gathers
@@ -369,11 +373,21 @@ csr_stream_kernel(const GatherArgs a)
                     }
                     break;
                 }
+                if (ends == 0) {
+                    // no row ends here: the batch is full and in one row
+#pragma unroll
+                    for (int j = 0; j < U; ++j)
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV) F::run(acc[q], vj[j], bv[j][q]);
+                    continue;
+                }
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
                     if (j < nvalid) {
 #pragma unroll
-                        for (int q = 0; q < VPL; ++q) F::run(acc[q], vj[j], bv[j][q]);
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV) F::run(acc[q], vj[j], bv[j][q]);
                     }
                     if ((ends >> j) & 1u) {
                         if (head_pending || ((tails >> j) & 1u)) {
@@ -482,8 +496,11 @@ template <typename T, typename I, int G, int VPL, int U, int MINB>
 cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
 {
     if constexpr (G >= 16) {
-        if (!prefer_row_kernel())
-            return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB>, a, 32 / G, stream);
+        if (!prefer_row_kernel() && a.K > 0) {
+            if (a.N / Vec<T>::kElems == G * VPL)
+                return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB, true>, a, 32 / G, stream);
+            return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB, false>, a, 32 / G, stream);
+        }
     }
     return launch_kernel<T, I>(csr_gather_kernel<T, I, G, VPL, U, (G >= 16 && MINB < 3 && VPL == 1) ? MINB + 1 : MINB>,
                                a, 1, stream);
