@@ -417,6 +417,279 @@ csr_stream_kernel(const GatherArgs a)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Ring kernel: the stream kernel with its gathers landing in shared memory.
+//
+// Each lane copies the 16-byte pieces of the B rows it will itself consume
+// (cp.async.cg, L2 only) into a per-group ring of 2 x U positions and reads
+// them back with one 16-byte shared load per position: no cross-lane
+// synchronisation is needed (cp.async.wait_group covers the thread's own
+// copies), in-flight data holds no registers, so more groups fit per SM and
+// two batches stay in flight.  Row bookkeeping and the per-row fma order are
+// those of csr_stream_kernel, so results are bitwise identical.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem)
+{
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16_cg_s(unsigned saddr, const void *gmem)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ uint4 lds16(unsigned saddr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(saddr));
+    return v;
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
+
+template <typename T, typename I, int G, int VPL, int U, int MINB, bool FULL>
+__global__ void __launch_bounds__(kGatherThreads, MINB)
+csr_ring_kernel(const GatherArgs a)
+{
+    static_assert(G == 16 || G == 32, "ring groups are half-warps or warps");
+    using F = FmaVec<T>;
+    using Scalar = typename F::Scalar;
+    constexpr int S = 32 / G;
+    constexpr int EPV = Vec<T>::kElems;
+    constexpr int CH = 64;          // nonzeros per prefetched column/value chunk
+    constexpr int PER = CH / G;
+    constexpr int RING = 2 * U;     // positions in the ring (two batches)
+    static_assert(CH % U == 0 && U <= G, "batches tile the chunk");
+    extern __shared__ __align__(16) uint4 ring_smem[];
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / G, gl = lane % G, shift = sub * G;
+    const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << shift);
+    const int group_in_block = (threadIdx.x >> 5) * S + sub;
+    // this lane's column of the ring, as a 32-bit shared address
+    const unsigned ring_s = (unsigned)__cvta_generic_to_shared(ring_smem + (size_t)group_in_block * RING * VPL * G + gl);
+    const int64_t stream = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * S + sub;
+    const int64_t nstreams = (((int64_t)gridDim.x * blockDim.x) >> 5) * S;
+
+    const I *rowptr = static_cast<const I *>(a.rowptr);
+    const I *col = static_cast<const I *>(a.col);
+    const T *val = static_cast<const T *>(a.val);
+    const uint4 *Bl = static_cast<const uint4 *>(a.B) + gl;
+    uint4 *out = static_cast<uint4 *>(a.out);
+    const int NV = (int)(a.N / EPV);
+
+    for (int64_t u = a.unit_begin + stream; u < a.unit_end; u += nstreams) {
+        const int64_t lo = u * a.unit;
+        const int64_t hi = min(lo + a.unit, a.nnz);
+        const bool last = (u == a.unit_end - 1);
+        const int64_t i0 = group_lower_bound<I, G>(rowptr, a.row_begin, a.M + 1, lo, gmask, gl, shift);
+        int64_t r = i0;
+        if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r = i0 - 1;
+
+        int64_t rc = r;
+        int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
+        int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+        auto rp = [&](int64_t x) -> int64_t {
+            if (x < rc || x >= rc + 2 * G) {
+                rc = x;
+                rpa = ld_idx(rowptr + min(rc + gl, a.M));
+                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+            } else if (x >= rc + G) {
+                rc += G;
+                rpa = rpb;
+                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+            }
+            return __shfl_sync(gmask, rpa, (int)(x - rc), G);
+        };
+        auto zero_row = [&](int64_t row) {
+#pragma unroll
+            for (int q = 0; q < VPL; ++q) {
+                const int vi = gl + q * G;
+                if (FULL || vi < NV) __stcs(out + row * NV + vi, make_uint4(0, 0, 0, 0));
+            }
+        };
+
+        int64_t beg = 0, end = 0;
+        bool have_row = false;
+        for (; r < a.M; ++r) {
+            beg = rp(r);
+            end = rp(r + 1);
+            if (beg < 0 || end < beg || end > a.nnz) {
+                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                break;
+            }
+            if (beg >= hi && !last) break;
+            if (end > beg) { have_row = true; break; }
+            zero_row(r);
+        }
+        if (!have_row) continue;
+        const int64_t s0 = max(lo, beg);
+        bool head_pending = beg < lo;
+        const int nbatch = (int)((hi - s0 + U - 1) / U);
+
+        float acc[VPL][EPV];
+#pragma unroll
+        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+
+        // column/value chunks: A holds chunk ka, B chunk ka + 1
+        int colA[PER], colB[PER];
+        Scalar valA[PER], valB[PER];
+        auto load_chunk = [&](int64_t pos, int *cc, Scalar *vv) {
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int64_t e = pos + gl + k * G;
+                cc[k] = 0;
+                vv[k] = F::zero();
+                if (e < hi) {
+                    const int64_t c = (int64_t)ld_stream(col + e);
+                    if (c >= 0 && c < a.K) {
+                        cc[k] = (int)c;
+                        vv[k] = F::load(val + e);
+                    } else {
+                        raise_status(a.status, SPMM_DEV_BAD_COLUMN, e);
+                    }
+                }
+            }
+        };
+        int ka = 0;
+        load_chunk(s0, colA, valA);
+        load_chunk(s0 + CH, colB, valB);
+        // Entry o (offset from s0) lives in chunk o / CH (A = chunk ka,
+        // B = chunk ka + 1), register slot (o % CH) / G, lane o % G.  A batch
+        // never straddles a slot (U divides G), so the register is chosen once
+        // per batch and each entry costs one shuffle.
+        auto pick_col = [&](int o0) -> int {
+            const bool inA = (o0 / CH) == ka;
+            const int slot = (o0 % CH) / G;
+            int cw = inA ? colA[0] : colB[0];
+#pragma unroll
+            for (int k = 1; k < PER; ++k)
+                if (slot == k) cw = inA ? colA[k] : colB[k];
+            return cw;
+        };
+        auto pick_val = [&](int o0) -> Scalar {
+            const bool inA = (o0 / CH) == ka;
+            const int slot = (o0 % CH) / G;
+            Scalar vw = inA ? valA[0] : valB[0];
+#pragma unroll
+            for (int k = 1; k < PER; ++k)
+                if (slot == k) vw = inA ? valA[k] : valB[k];
+            return vw;
+        };
+        auto issue = [&](int k) {
+            if (k < nbatch) {
+                const int o0 = k * U;
+                const int nv = (int)min((int64_t)U, hi - (s0 + o0));
+                const int cw = pick_col(o0);
+                const unsigned slot0 = ring_s + (unsigned)((k & 1) * U * VPL * G * 16);
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int c = __shfl_sync(gmask, cw, (o0 + j) % G, G);
+                    if (j < nv) {
+                        const uint4 *src = Bl + (int64_t)c * NV;
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV) cp_async16_cg_s(slot0 + (j * VPL + q) * G * 16, src + q * G);
+                    }
+                }
+            }
+            cp_async_commit_group();
+        };
+        issue(0);
+        issue(1);
+
+        bool done = false;
+        for (int k = 0; k < nbatch && !done; ++k) {
+            const int64_t pbase = s0 + (int64_t)k * U;
+            const int nvalid = (int)min((int64_t)U, hi - pbase);
+            const int64_t bend = pbase + nvalid;
+            // row bookkeeping of this batch (as in csr_stream_kernel)
+            unsigned ends = 0, tails = 0;
+            int64_t myrow = 0;
+            for (;;) {
+                if (end <= bend) {
+                    const int jb = (int)(end - pbase - 1);
+                    ends |= 1u << jb;
+                    if (gl == jb) myrow = r;
+                    const int64_t prev = end;
+                    bool next = false;
+                    for (++r; r < a.M; ++r) {
+                        beg = prev;
+                        end = rp(r + 1);
+                        if (end < beg || end > a.nnz) {
+                            if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                            break;
+                        }
+                        if (beg >= hi && !last) break;
+                        if (end > beg) { next = true; break; }
+                        zero_row(r);
+                    }
+                    if (!next) { done = true; break; }
+                    continue;
+                }
+                if (bend == hi) {
+                    ends |= 1u << (nvalid - 1);
+                    tails |= 1u << (nvalid - 1);
+                    if (gl == nvalid - 1) myrow = r;
+                    done = true;
+                }
+                break;
+            }
+            cp_async_wait_1();   // this lane's copies of batch k have landed
+            const unsigned slot0 = ring_s + (unsigned)((k & 1) * U * VPL * G * 16);
+            const Scalar vw = pick_val(k * U);
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                if (j < nvalid) {
+                    const Scalar v = __shfl_sync(gmask, vw, (k * U + j) % G, G);
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q)
+                        if (FULL || gl + q * G < NV) F::run(acc[q], v, lds16(slot0 + (j * VPL + q) * G * 16));
+                }
+                if ((ends >> j) & 1u) {
+                    if (head_pending || ((tails >> j) & 1u)) {
+                        float *prow = a.partial + ((u - a.unit_begin) * 2 + (head_pending ? 0 : 1)) * a.N;
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q) {
+                            const int vi = gl + q * G;
+                            if (!FULL && vi >= NV) continue;
+                            float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+#pragma unroll
+                            for (int e = 0; e < EPV; e += 4)
+                                dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                        }
+                        head_pending = false;
+                    } else {
+                        const int64_t row = __shfl_sync(gmask, myrow, j, G);
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q) {
+                            const int vi = gl + q * G;
+                            if (FULL || vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                        for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                }
+            }
+            // consumption moves to the next chunk: B becomes A and the chunk
+            // after it is loaded, 6 batches before the issue stage needs it
+            if (((k + 1) * U) % CH == 0) {
+#pragma unroll
+                for (int i = 0; i < PER; ++i) {
+                    colA[i] = colB[i];
+                    valA[i] = valB[i];
+                }
+                ++ka;
+                load_chunk(s0 + (int64_t)(ka + 1) * CH, colB, valB);
+            }
+            issue(k + 2);
+        }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+    }
+}
+
 // Sums the per-unit partials of every row that crosses a unit boundary, in
 // unit order: tail(u0) + head(u0 + 1) + ... + head(u1).  One warp per unit;
 // a unit owns the fix-up of the split row that starts inside it.
@@ -480,24 +753,61 @@ cudaError_t launch_kernel(Kern kern, const GatherArgs &a, int64_t units_per_warp
     return e;
 }
 
-// Kernel choice for rows of >= 16 vectors: the flat-stream kernel unless the
-// environment variable SPMM_B200_GATHER=row selects the row kernel (both
-// produce identical sums; the knob exists for A/B measurement).
-bool prefer_row_kernel()
+// Kernel choice for rows of >= 16 vectors (all produce identical sums; the
+// environment variable SPMM_B200_GATHER = ring | stream | row selects one for
+// A/B measurement).
+int gather_kernel_choice()
 {
-    static const bool row = [] {
+    static const int choice = [] {
         const char *v = getenv("SPMM_B200_GATHER");
-        return v && strcmp(v, "row") == 0;
+        if (v && strcmp(v, "row") == 0) return 2;
+        if (v && strcmp(v, "stream") == 0) return 1;
+        return 0;
     }();
-    return row;
+    return choice;
+}
+
+template <typename T, typename I, typename Kern>
+cudaError_t launch_ring(Kern kern, const GatherArgs &a, int units_per_warp, size_t smem, cudaStream_t stream)
+{
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGatherThreads, smem);
+    if (e != cudaSuccess) return e;
+    const int64_t units = a.unit_end - a.unit_begin;
+    const int64_t warps_needed = (units + units_per_warp - 1) / units_per_warp;
+    int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
+    blocks = std::max<int64_t>(1, std::min(blocks, (warps_needed + 7) / 8));
+    kern<<<(unsigned)blocks, kGatherThreads, smem, stream>>>(a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    if (units > 1) {
+        const int64_t fb = std::min<int64_t>((units + 7) / 8, 8LL * device_sm_count());
+        csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
+        e = cudaGetLastError();
+    }
+    return e;
 }
 
 template <typename T, typename I, int G, int VPL, int U, int MINB>
 cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
 {
     if constexpr (G >= 16) {
-        if (!prefer_row_kernel() && a.K > 0) {
-            if (a.N / Vec<T>::kElems == G * VPL)
+        const int choice = gather_kernel_choice();
+        const bool full = a.N / Vec<T>::kElems == G * VPL;
+        if (choice == 0 && a.K > 0 && G == 32) {
+            // ring (measured faster when a whole warp serves one row; half-warp
+            // groups stay on the stream kernel): 2 * U positions x VPL
+            // vectors per lane, 8 warps per block
+            const size_t smem = (size_t)kGatherThreads * 2 * U * VPL * 16;
+            constexpr int RMINB = (VPL == 1) ? 3 : 2;
+            if (full)
+                return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, true>, a, 32 / G, smem, stream);
+            return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, false>, a, 32 / G, smem, stream);
+        }
+        if (choice <= 1 && a.K > 0) {
+            if (full)
                 return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB, true>, a, 32 / G, stream);
             return launch_kernel<T, I>(csr_stream_kernel<T, I, G, VPL, U, MINB, false>, a, 32 / G, stream);
         }
