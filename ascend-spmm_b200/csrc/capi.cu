@@ -251,6 +251,52 @@ int spmm_ascend_cube_aiv_mb_launch(SPMM_MIXED_ARGS)
     return mixed_impl(SPMM_MIXED_FORWARD, 1, 1, "spmm_ascend_cube_aiv_mb");
 }
 
+size_t spmm_cube_workspace_bytes(int64_t n_windows, int64_t nnz, int64_t N, int itype, int dtype)
+{
+    (void)N;
+    if (n_windows <= 0) return 0;
+    return spmmb::cube_workspace_bytes(n_windows, nnz, itype, dtype);
+}
+
+int spmm_cube_launch(const void *rowptr, const void *col, const void *value, const void *dense,
+                     const int32_t *start, int64_t n_start, void *out, int64_t n_windows, int64_t K, int64_t N,
+                     int64_t nnz, int itype, int dtype, void *workspace, size_t workspace_bytes, void *stream)
+{
+    (void)start;
+    (void)n_start;
+    const char *op = "spmm_cube";
+    int rc = check_dense(dtype, N, 16, op);   // custom_op.cpp:102
+    if (rc) return rc;
+    if ((rc = check_itype(itype, op))) return rc;
+    if (n_windows < 0 || K < 0 || nnz < 0) return set_error(SPMM_ERR_ARG, "%s: negative size", op);
+    if (n_windows == 0) return SPMM_OK;
+    if (!rowptr || !dense || !out || (nnz > 0 && (!col || !value)))
+        return set_error(SPMM_ERR_ARG, "%s: null array", op);
+    if (misaligned(dense) || misaligned(out) || misaligned(workspace))
+        return set_error(SPMM_ERR_ARG, "%s: dense, out and workspace must be 16-byte aligned", op);
+    const size_t need = spmmb::cube_workspace_bytes(n_windows, nnz, itype, dtype);
+    if (workspace_bytes < need || !workspace)
+        return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
+                         workspace_bytes, need);
+    cudaError_t e;
+    spmmb::DevStatus *st = spmmb::device_status_ptr(&e);
+    if (!st) return cuda_error(e, op);
+    spmmb::CubeArgs a{};
+    a.rowptr = rowptr; a.col = col; a.val = value; a.B = dense; a.out = out;
+    a.nwin = n_windows; a.K = K; a.N = N; a.nnz = nnz; a.status = st;
+    e = spmmb::launch_cube(a, itype, dtype, workspace, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, op);
+    return SPMM_OK;
+}
+
+int spmm_csr_to_spmm_cube_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                              int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
+                              spmm_layout *out, void *stream)
+{
+    return spmmb::pre_csr_to_spmm_cube(crow, col, val, nrows, ncols, nnz, window_size, itype, vbytes, alloc, out,
+                                       stream);
+}
+
 int spmm_csr_to_bcsr_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
                          int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
                          spmm_layout *out, void *stream)

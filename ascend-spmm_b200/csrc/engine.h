@@ -83,6 +83,24 @@ struct WindowArgs {
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined,
                           cudaStream_t stream);
 
+// ---- spmm_cube (cube.cu) -----------------------------------------------------
+
+struct CubeArgs {
+    const void *rowptr;  // [nwin + 1] entry offsets of each 16-row window
+    const void *col;     // [nnz] (column << 4) | row
+    const void *val;     // [nnz]
+    const void *B;
+    void *out;           // [16 * nwin, N]
+    int64_t nwin;
+    int64_t K;
+    int64_t N;
+    int64_t nnz;
+    DevStatus *status;
+};
+
+size_t cube_workspace_bytes(int64_t nwin, int64_t nnz, int itype, int dtype);
+cudaError_t launch_cube(const CubeArgs &a, int itype, int dtype, void *workspace, cudaStream_t stream);
+
 // ---- row permutation copies (rows.cu) ---------------------------------------
 
 cudaError_t launch_pack_rows(const void *src, const int64_t *inv, int64_t n, int64_t row_bytes, void *dst,
@@ -95,6 +113,9 @@ cudaError_t launch_restore_rows(const void *src, int64_t src_rows, const int64_t
 int pre_csr_to_bcsr(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols, int64_t nnz,
                     int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc, spmm_layout *out,
                     void *stream, bool cube);
+int pre_csr_to_spmm_cube(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                         int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
+                         spmm_layout *out, void *stream);
 int pre_block_level_split(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
                           int64_t nnz, double a, int64_t window_size, int itype, int vbytes,
                           const spmm_allocator *alloc, spmm_layout *out, void *stream);

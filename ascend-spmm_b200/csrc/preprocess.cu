@@ -889,6 +889,74 @@ void build_bcsr(Ctx &c, const I *rowptr, const I *col, const void *val, int64_t 
     set_array(out->value, value, 256 * T);
 }
 
+// ---- producer of the spmm_cube window encoding ------------------------------
+
+template <typename I, typename W>
+__global__ void cube_encode_kernel(const uint64_t *sk, const int64_t *sp, int64_t n, int cbits, const void *val,
+                                   I *col_out, void *val_out)
+{
+    const uint64_t cmask = (uint64_t(1) << cbits) - 1;
+    GRID_STRIDE(i, n)
+    {
+        const uint64_t k = sk[i];
+        col_out[i] = (I)((((k >> 4) & cmask) << 4) | (k & 15));
+        copy_val<W>(val_out, i, val, sp[i]);
+    }
+}
+
+template <typename I>
+__global__ void cube_window_ptr_kernel(const I *rowptr, int64_t nrows, int64_t nwin, I *out)
+{
+    GRID_STRIDE(w, nwin + 1) out[w] = rowptr[std::min<int64_t>(16 * w, nrows)];
+}
+
+// Sorting by (window, column, row) with a stable radix sort puts each
+// window's entries in ToBCSR's merge order (custom_op.cpp:611-671); the
+// window's entries keep their CSR offsets, so the window pointer is the CSR
+// row pointer sampled every 16 rows.
+template <typename I>
+void build_spmm_cube(Ctx &c, const I *rowptr, const I *col, const void *val, int64_t nrows, int64_t ncols,
+                     int64_t nnz, int vbytes, spmm_layout *out)
+{
+    const char *op = "csr_to_spmm_cube";
+    if (sizeof(I) == 4 && ncols > (int64_t(1) << 27)) {
+        c.fail(SPMM_ERR_ARG, "%s: int32 (column << 4 | row) needs ncols <= 2^27, got %lld", op, (long long)ncols);
+        return;
+    }
+    const int64_t nwin = (nrows + 15) / 16;
+    const int cbits = bits_for(std::max<int64_t>(ncols - 1, 0));
+    const int wbits = bits_for(std::max<int64_t>(nwin - 1, 0));
+    if (cbits + wbits + 4 > 64) {
+        c.fail(SPMM_ERR_UNSUPPORTED, "%s: matrix too large for 64-bit sort keys", op);
+        return;
+    }
+    I *wptr = c.out<I>(nwin + 1);
+    I *ecol = c.out<I>(nnz);
+    void *eval = c.raw((size_t)std::max<int64_t>(nnz, 1) * vbytes, true);
+    if (!c.ok()) return;
+    if (nrows == 0) {
+        c.zero(wptr, sizeof(I));
+    } else {
+        uint64_t *keys = c.tmp<uint64_t>(nnz), *sk = c.tmp<uint64_t>(nnz);
+        int64_t *vals = c.tmp<int64_t>(nnz), *sp = c.tmp<int64_t>(nnz);
+        if (!c.ok()) return;
+        make_keys_kernel<I><<<grid_for(nrows * 32), kThreads, 0, c.s>>>(rowptr, col, nrows, ncols, nnz, cbits, false,
+                                                                           keys, vals, c.dstat);
+        c.launched("make_keys");
+        if (!c.check_device(op)) return;
+        sort_pairs(c, keys, sk, vals, sp, nnz, cbits + wbits + 4);
+        cube_window_ptr_kernel<I><<<grid_for(nwin + 1), kThreads, 0, c.s>>>(rowptr, nrows, nwin, wptr);
+        dispatch_w(vbytes, [&](auto w) {
+            using W = decltype(w);
+            if (nnz > 0) cube_encode_kernel<I, W><<<grid_for(nnz), kThreads, 0, c.s>>>(sk, sp, nnz, cbits, val, ecol, eval);
+        });
+        c.launched(op);
+    }
+    set_array(out->crow_window_ptr, wptr, nwin + 1);
+    set_array(out->unique_col_ids, ecol, nnz);
+    set_array(out->value, eval, nnz);
+}
+
 template <typename I>
 void build_bls(Ctx &c, const I *rowptr, const I *col, const void *val, int64_t nrows, int64_t ncols, int64_t nnz,
                int vbytes, double a, spmm_layout *out)
@@ -1166,6 +1234,22 @@ int pre_csr_to_bcsr(const void *crow, const void *col, const void *val, int64_t 
                          else
                              build_bcsr<int64_t>(c, (const int64_t *)crow, (const int64_t *)col, val, nrows, ncols, nnz,
                                                  vbytes, cube, out);
+                     });
+}
+
+int pre_csr_to_spmm_cube(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
+                         int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
+                         spmm_layout *out, void *stream)
+{
+    *out = spmm_layout{};
+    return run_entry(alloc, stream, itype, vbytes, nrows, ncols, nnz, window_size, false, "csr_to_spmm_cube",
+                     [&](Ctx &c) {
+                         if (itype == SPMM_I32)
+                             build_spmm_cube<int>(c, (const int *)crow, (const int *)col, val, nrows, ncols, nnz, vbytes,
+                                                  out);
+                         else
+                             build_spmm_cube<int64_t>(c, (const int64_t *)crow, (const int64_t *)col, val, nrows, ncols,
+                                                      nnz, vbytes, out);
                      });
 }
 

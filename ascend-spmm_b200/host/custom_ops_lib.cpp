@@ -245,6 +245,44 @@ at::Tensor spmm_ascend_cube_aiv_mb_impl(MIXED_SIG)
 }
 
 // ---------------------------------------------------------------------------
+// spmm_cube (custom_op.cpp:91-113): windows of (column << 4 | row) entries.
+// ---------------------------------------------------------------------------
+at::Tensor spmm_cube_impl(const at::Tensor &rowptr, const at::Tensor &col, const at::Tensor &value,
+                          const at::Tensor &dense, const at::Tensor &start)
+{
+    TORCH_CHECK_CUDA(rowptr);
+    TORCH_CHECK_CUDA(col);
+    TORCH_CHECK_CUDA(value);
+    TORCH_CHECK_CUDA(dense);
+    TORCH_CHECK_CUDA(start);
+    TORCH_CHECK(rowptr.dim() == 1, "row must be a 1D Tensor, but got: ", rowptr.dim());
+    TORCH_CHECK(col.dim() == 1, "col must be a 1D Tensor, but got: ", col.dim());
+    TORCH_CHECK(value.dim() == 1, "value must be a 1D Tensor, but got: ", value.dim());
+    TORCH_CHECK(dense.dim() == 2, "dense must be a 2D Tensor, but got: ", dense.dim());
+    TORCH_CHECK(start.dim() == 1, "start must be a 1D Tensor, but got: ", start.dim());
+    check_dense_contract(dense, 16, "spmm_cube");
+    check_value_contract(value, dense, "value");
+    TORCH_CHECK(col.size(0) == value.size(0), "col and value must be same size, but got different: ",
+                col.size(0) - value.size(0));
+    TORCH_CHECK(rowptr.size(0) >= 1, "spmm_cube: rowptr must hold windows + 1 entries");
+    same_device({&rowptr, &col, &value, &start}, dense, "spmm_cube");
+    const int itype = index_code({&rowptr, &col}, "spmm_cube");
+    c10::cuda::CUDAGuard guard(dense.device());
+
+    const int64_t nwin = rowptr.size(0) - 1, D = dense.size(1), nnz = col.size(0);
+    at::Tensor result = at::empty({nwin * 16, D}, dense.options());
+    const int dt = dtype_code(dense);
+    const size_t wbytes = spmm_cube_workspace_bytes(nwin, nnz, D, itype, dt);
+    at::Tensor ws = workspace(wbytes, dense);
+    at::Tensor start_i = start.to(at::kInt).contiguous();
+    const at::Tensor B = aligned16(dense);
+    check_rc(spmm_cube_launch(rowptr.data_ptr(), col.data_ptr(), value.data_ptr(), B.data_ptr(),
+                              start_i.data_ptr<int32_t>(), start_i.numel(), result.data_ptr(), nwin, dense.size(0), D,
+                              nnz, itype, dt, ws.data_ptr(), wbytes, stream_of(dense)));
+    return result;
+}
+
+// ---------------------------------------------------------------------------
 // Layout builders: csr_to_bcsr, csr_to_ascend_cube, block_level_split,
 // preprocess (custom_op.cpp:429-1412).  Same argument order and dict keys as
 // the reference; inputs may be CPU or CUDA tensors (CPU inputs are copied to
@@ -380,6 +418,25 @@ std::map<std::string, at::Tensor> csr_to_ascend_cube(at::Tensor crow_ptr, at::Te
     return d;
 }
 
+// Producer of spmm_cube's input: {"rowptr", "col", "value"}.
+std::map<std::string, at::Tensor> csr_to_spmm_cube(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
+                                                   int64_t nrows, int64_t ncols, int64_t window_size)
+{
+    CsrInput in = prepare_csr(crow_ptr, col_indices, values, "csr_to_spmm_cube");
+    check_rows(in, nrows, "csr_to_spmm_cube");
+    c10::cuda::CUDAGuard guard(in.crow.device());
+    TorchAllocator A(in.crow.device());
+    spmm_layout L{};
+    check_pre(spmm_csr_to_spmm_cube_run(in.crow.data_ptr(), in.col.data_ptr(), in.val.data_ptr(), nrows, ncols,
+                                        in.col.size(0), window_size, in.itype, in.vbytes, &A.handle, &L,
+                                        stream_of(in.crow)));
+    std::map<std::string, at::Tensor> d;
+    d["rowptr"] = A.take(L.crow_window_ptr, crow_ptr.scalar_type());
+    d["col"] = A.take(L.unique_col_ids, crow_ptr.scalar_type());
+    d["value"] = A.take(L.value, values.scalar_type());
+    return d;
+}
+
 std::map<std::string, at::Tensor> block_level_split(at::Tensor crow_ptr, at::Tensor col_indices, at::Tensor values,
                                                     int64_t nrows, int64_t ncols, double a, int64_t window_size)
 {
@@ -484,6 +541,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m)
 {
     m.def("spmm_csr", &spmm_csr_impl,
           "CUDA CSR SpMM; FP16 width divisible by 16 with MAXD=1024, FP32 width divisible by 8 with MAXD=512");
+    m.def("spmm_cube", &spmm_cube_impl,
+          "CUDA window SpMM over (column << 4 | row) entries; width divisible by 16, MAXD=1024 for FP16 and 512 "
+          "for FP32");
     m.def("spmm_ascend_cube", &spmm_ascend_cube_impl,
           "CUDA mixed window/CSR SpMM; width divisible by 16, MAXD=1024 for FP16 and 512 for FP32");
     m.def("spmm_ascend_cube_aic_without_pipeline", &spmm_ascend_cube_aic_without_pipeline_impl,
@@ -508,6 +568,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m)
           "graph the P*A*P^T relabel and its fixed-layout transpose), bit-exact with the reference.",
           pybind11::arg("crow_ptr"), pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"),
           pybind11::arg("ncols"), pybind11::arg("window_size") = 16, pybind11::arg("graph_layout") = false);
+    m.def("csr_to_spmm_cube", &csr_to_spmm_cube,
+          "Encode CSR for spmm_cube on the GPU: dict with rowptr [nwindows + 1] (entry offsets per 16-row window), "
+          "col [nnz] = (column << 4) | row in (column, row) order per window, value [nnz]",
+          pybind11::arg("crow_ptr"), pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"),
+          pybind11::arg("ncols"), pybind11::arg("window_size") = 16);
     m.def("block_level_split", &block_level_split,
           "Split CSR into (16,1)-BSR + CSR hybrid dict by block density (GPU)", pybind11::arg("crow_ptr"),
           pybind11::arg("col_indices"), pybind11::arg("values"), pybind11::arg("nrows"), pybind11::arg("ncols"),

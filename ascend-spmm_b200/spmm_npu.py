@@ -20,18 +20,16 @@ from custom_ops_lib import (  # noqa: F401  (re-exported API)
     spmm_ascend_cube_aiv_mb,
     spmm_csr,
     spmm_csr_aiv_mb_batch,
+    spmm_cube,
 )
 
 from custom_ops_lib import (  # noqa: F401  (GPU layout builders)
     block_level_split,
     csr_to_ascend_cube,
     csr_to_bcsr,
+    csr_to_spmm_cube,
     preprocess,
 )
-try:
-    from custom_ops_lib import spmm_cube  # noqa: F401
-except ImportError:  # pragma: no cover
-    pass
 from custom_ops_lib import pack_rows as _pack_rows, restore_rows as _restore_rows
 
 
@@ -83,6 +81,7 @@ __all__ = [
     "block_level_split",
     "csr_to_ascend_cube",
     "csr_to_bcsr",
+    "csr_to_spmm_cube",
     "pack_node_tensor",
     "preprocess",
     "restore_node_tensor",

@@ -6,9 +6,15 @@
 
 One step = one SpMM C = A @ B of BASELINE config 2 (1M x 1M power-law graph,
 ~16 nonzeros/row, fp16, N = 256) with its inputs resident in HBM.  With N
-GPUs (torchrun, one rank per GPU) A is row-partitioned by nonzeros at 16-row
-window granularity, B is replicated and C stays row-sharded: no collective
-runs in the timed region (strong scaling: the total work is fixed).
+GPUs (torchrun, one rank per GPU) A is row-partitioned, B is replicated and C
+stays row-sharded: no collective runs in the timed region.
+
+``--scaling weak`` (default): every rank owns one config-sized row block of a
+global A of N blocks (rank r's block is the config generated with seed
+2027 + r; rank 0's block is the 1-GPU workload) times the shared B (seed
+2027), so the work per GPU is fixed as N grows.  ``--scaling strong``: the
+single config matrix is cut into N row ranges balanced by nonzeros at 16-row
+window boundaries (spmm_dist.shard_bounds).
 
 ``--impl reference`` times the reference's own CPU path for SpMM
 (tests/aic_aiv_ablation/common.py:173-177: torch.sparse.mm in fp32, all
@@ -55,6 +61,7 @@ def parse_args():
     p.add_argument("--config", type=int, default=2)
     p.add_argument("--scale", type=float, default=1.0)
     p.add_argument("--op", choices=("csr", "mixed"), default="csr")
+    p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
     p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -218,16 +225,23 @@ def run_ours(args, rank, world, local):
     import spmm_npu
 
     dev = torch.device("cuda", local)
-    w = workloads.make(args.config, device=dev, scale=args.scale)
-    nnz_global = w.nnz
     from spmm_dist import allgather_rows, shard_bounds
 
-    bounds = shard_bounds(w.rowptr, world)
-    r0, r1 = bounds[rank]
-    rp, col, val = workloads.row_slice(w, r0, r1)
+    if args.scaling == "weak":
+        w = workloads.make(args.config, device=dev, scale=args.scale, seed=workloads.DEFAULT_SEED + rank)
+        B = w.B if rank == 0 else workloads.make(args.config, device=dev, scale=args.scale).B
+        rp, col, val = w.rowptr, w.col, w.val
+        bounds = [(k * w.M, (k + 1) * w.M) for k in range(world)]
+        nnz_global = int(allreduce_sum(float(w.nnz), world))
+    else:
+        w = workloads.make(args.config, device=dev, scale=args.scale)
+        bounds = shard_bounds(w.rowptr, world)
+        r0, r1 = bounds[rank]
+        rp, col, val = workloads.row_slice(w, r0, r1)
+        B = w.B
+        nnz_global = w.nnz
     rp, col, val = rp.contiguous(), col.contiguous(), val.contiguous()
-    B = w.B
-    M_local, nnz_local = r1 - r0, int(col.numel())
+    M_local, nnz_local = int(rp.numel()) - 1, int(col.numel())
     start = torch.zeros(40, dtype=torch.int32, device=dev)
 
     mixed = None
@@ -294,9 +308,11 @@ def run_ours(args, rank, world, local):
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)" if s == 2 else "f32",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f16 (fp32 accumulate)" if s == 2 else "f32",
         "data": "synthetic (seeded generator, BASELINE config shapes)",
-        "config": {"workload": f"{w.name} M=K={w.M} nnz={nnz_global} N={w.N}",
+        "config": {"workload": (f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}" if args.scaling == "strong" or world == 1
+                                else f"{world} row blocks of {w.name} (M=K={w.M}, seeds {workloads.DEFAULT_SEED}"
+                                     f"+rank), {nnz_global} nnz in all, N={w.N}"),
                    "op": "spmm_csr" if mixed is None else "spmm_ascend_cube(preprocess)",
                    "parallelism": f"row-shard x{world} (B replicated, C row-sharded)",
                    "l2": f"inputs larger than L2 (B {B.numel() * B.element_size() / 1e6:.0f} MB), no flush",
@@ -406,7 +422,7 @@ def run_reference(args, rank, world):
     out = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded generator, BASELINE config shapes)",
         "config": {"workload": f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}", "op": "torch.sparse.mm (cpu_reference)",
                    "parallelism": f"host CPU, {threads} threads"},

@@ -152,6 +152,19 @@ int spmm_ascend_cube_aiv_mb_launch(
     int64_t n_blocks, int64_t v_rows, int64_t v_nnz, int64_t K, int64_t N, int itype,
     int dtype, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Replaces spmm_cube_impl_npu (custom_op.cpp:91-113; kernel
+ * op_kernel/spmm_cube.cpp:51-147).  rowptr [n_windows + 1] holds the entry
+ * offsets of each 16-row window; col[i] = (column << 4) | row; output
+ * [16 * n_windows, N].  Inside a window, a run of entries with equal column
+ * is one (16 x 1) block and the last entry of a row in a run wins.  fp16
+ * and fp32 widths: N % 16 == 0 (custom_op.cpp:102).  The workspace holds the
+ * normalised block stream (bounded by nnz blocks). */
+size_t spmm_cube_workspace_bytes(int64_t n_windows, int64_t nnz, int64_t N, int itype, int dtype);
+int spmm_cube_launch(const void *rowptr, const void *col, const void *value, const void *dense,
+                     const int32_t *start, int64_t n_start, void *out, int64_t n_windows, int64_t K,
+                     int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
+                     size_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------------- */
 /* Layout builders (GPU, bit-exact with the reference's CPU preprocessing). */
 /* Inputs: CSR on the device (crow [nrows + 1], col [nnz], val [nnz] with  */
@@ -200,6 +213,16 @@ int spmm_csr_to_bcsr_run(const void *crow, const void *col, const void *val, int
 int spmm_csr_to_ascend_cube_run(const void *crow, const void *col, const void *val, int64_t nrows,
                                 int64_t ncols, int64_t nnz, int64_t window_size, int itype, int vbytes,
                                 const spmm_allocator *alloc, spmm_layout *out, void *stream);
+
+/* Producer of spmm_cube's input (the reference ships the consumer only):
+ * crow_window_ptr [nwin + 1] = crow[min(16 w, nrows)], unique_col_ids [nnz]
+ * = (column << 4) | row with each window's entries in (column, row) order
+ * (ToBCSR's merge order, custom_op.cpp:611-671; equal pairs keep CSR
+ * order), value [nnz].  vrow/vcol/vvalue stay empty.  With int32 indices
+ * ncols must be <= 2^27 so the encoding fits. */
+int spmm_csr_to_spmm_cube_run(const void *crow, const void *col, const void *val, int64_t nrows,
+                              int64_t ncols, int64_t nnz, int64_t window_size, int itype, int vbytes,
+                              const spmm_allocator *alloc, spmm_layout *out, void *stream);
 
 /* Replaces block_level_split / hybrid_split_impl (custom_op.cpp:1146-1348,
  * 1390-1412): the k least-dense blocks move to CSR, k = first argmin of

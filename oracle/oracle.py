@@ -15,9 +15,11 @@ Contents
   with the reference's dtypes: index arrays follow the input index dtype,
   values follow the input value dtype, ``permutation``/``inv_permutation`` and
   audit counters are int64 and costs float64 (custom_op.cpp:1037-1109).
-* ``spmm_csr_f64`` / ``spmm_mixed_f64``: the SpMM semantics of the reference
+* ``csr_to_spmm_cube``: the producer of ``spmm_cube``'s window encoding
+  (the reference has the consumer only) in ToBCSR's merge order.
+* ``spmm_csr_f64`` / ``spmm_mixed_f64`` / ``spmm_cube_f64``: the SpMM semantics of the reference
   kernels (op_kernel/spmm_csr.cpp:383-423; op_kernel/spmm_ascend_cube.cpp:52-165,
-  265-288, 782-875) evaluated in float64 on the (already fp16/fp32-rounded)
+  265-288, 782-875; op_kernel/spmm_cube.cpp:51-147) evaluated in float64 on the (already fp16/fp32-rounded)
   inputs - the same construction as the reference's unused
   ``cpu_reference`` (tests/aic_aiv_ablation/common.py:173-177).
 * ``cpu_reference``: that reference function restated (torch.sparse.mm in
@@ -114,6 +116,8 @@ def lib():
         dp = ctypes.POINTER(ctypes.c_double)
         _lib.orc_spmm_csr_f64.argtypes = [ctypes.c_int64, ctypes.c_int64, _I64P, _I64P, dp, dp, dp]
         _lib.orc_spmm_window_f64.argtypes = [ctypes.c_int64, ctypes.c_int64, _I64P, _I64P, dp, dp, dp]
+        _lib.orc_spmm_cube_f64.argtypes = [ctypes.c_int64, ctypes.c_int64, _I64P, _I64P, dp, dp, dp]
+        _lib.orc_csr_to_spmm_cube.argtypes = common + [ctypes.c_int64, ctypes.POINTER(_Layout)]
     return _lib
 
 
@@ -230,6 +234,23 @@ def block_level_split(crow_ptr, col_indices, values, nrows, ncols, a, window_siz
         lib().orc_free_layout(ctypes.byref(o))
 
 
+def csr_to_spmm_cube(crow_ptr, col_indices, values, nrows, ncols, window_size=16) -> dict:
+    """Producer of the ``spmm_cube`` input (keys ``rowptr``, ``col``, ``value``):
+    per 16-row window the entries in (column, row) order, ``col`` holding
+    ``(column << 4) | row``.  The reference ships only the consumer
+    (op_kernel/spmm_cube.cpp:51-147); the order is ToBCSR's merge order
+    (custom_op.cpp:611-671)."""
+    crow, col, raw, esz, vdt, idx = _prep(crow_ptr, col_indices, values)
+    o = _Layout()
+    _check(lib().orc_csr_to_spmm_cube(nrows, ncols, col.size, _ptr(crow), _ptr(col),
+                                      raw.ctypes.data, esz, window_size, ctypes.byref(o)))
+    try:
+        d = _layout_dict(o, idx, esz, vdt, with_v=False)
+        return {"rowptr": d["crow_window_ptr"], "col": d["unique_col_ids"], "value": d["value"]}
+    finally:
+        lib().orc_free_layout(ctypes.byref(o))
+
+
 def preprocess(crow_ptr, col_indices, values, nrows, ncols, window_size=16,
                graph_layout=False) -> dict:
     crow, col, raw, esz, vdt, idx = _prep(crow_ptr, col_indices, values)
@@ -301,6 +322,18 @@ def spmm_mixed_f64(Crowptr, Ccol_ids, Cvalue, Vrowptr, Vcol_ids, Vvalue, dense) 
     return y
 
 
+def spmm_cube_f64(rowptr, col, value, dense) -> np.ndarray:
+    """Output of ``spmm_cube`` in float64 ([16 * #windows, N]): runs of equal
+    column inside a window form one (16 x 1) block, the last entry of a row in
+    a run wins (op_kernel/spmm_cube.cpp:51-147)."""
+    rp, c, v, B = _i64(rowptr), _i64(col), _f64(value), _f64(dense)
+    nwin, n = rp.size - 1, B.shape[1]
+    y = np.zeros((16 * nwin, n), np.float64)
+    dp = ctypes.POINTER(ctypes.c_double)
+    lib().orc_spmm_cube_f64(nwin, n, _ptr(rp), _ptr(c), _ptr(v, dp), _ptr(B, dp), _ptr(y, dp))
+    return y
+
+
 def cpu_reference(rows, cols, crow, col, values, dense) -> torch.Tensor:
     """tests/aic_aiv_ablation/common.py:173-177 restated: torch.sparse.mm in fp32."""
     matrix = torch.sparse_csr_tensor(crow, col, values.float(), size=(rows, cols),
@@ -326,5 +359,5 @@ def tolerance(dtype: torch.dtype) -> tuple[float, float]:
 
 __all__ = [
     "build", "csr_to_bcsr", "csr_to_ascend_cube", "block_level_split", "preprocess",
-    "spmm_csr_f64", "spmm_mixed_f64", "cpu_reference", "make_start", "tolerance",
+    "csr_to_spmm_cube", "spmm_csr_f64", "spmm_mixed_f64", "spmm_cube_f64", "cpu_reference", "make_start", "tolerance",
 ]

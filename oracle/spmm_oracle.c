@@ -601,3 +601,102 @@ void orc_spmm_window_f64(int64_t nwin, int64_t n, const int64_t *cptr, const int
             }
         }
 }
+
+/* ------------------------------------------------------------------------ */
+/* spmm_cube: window entries encoded as (column << 4) | row.                 */
+/* ------------------------------------------------------------------------ */
+
+/* The reference kernel (kernels/op_kernel/spmm_cube.cpp:51-147) walks the
+ * entries of window w = [rowptr[w], rowptr[w+1]) in order.  An entry whose
+ * column (col >> 4) differs from the previous entry's opens a new (16 x 1)
+ * block (spmm_cube.cpp:88-107; the first entry of a window always does,
+ * :77); the entry's value is stored at row (col & 15) of that block,
+ * overwriting an earlier entry of the same row in the same block (:125-126).
+ * Every block adds block[r] * B[column, :] to output row 16 w + r
+ * (:210, :235-236).  y must hold 16 * nwin * n zeros on entry. */
+void orc_spmm_cube_f64(int64_t nwin, int64_t n, const int64_t *rowptr, const int64_t *col,
+                       const double *val, const double *B, double *y)
+{
+    double a[16];
+    int set[16];
+    for (int64_t w = 0; w < nwin; ++w) {
+        int64_t cur = 0;
+        int open = 0;
+        for (int64_t p = rowptr[w]; p <= rowptr[w + 1]; ++p) {
+            const int end = p == rowptr[w + 1];
+            const int64_t c = end ? 0 : (col[p] >> 4);
+            if (open && (end || c != cur)) {
+                const double *brow = B + cur * n;
+                for (int r = 0; r < 16; ++r) {
+                    if (!set[r]) continue;
+                    double *yr = y + (16 * w + r) * n;
+                    for (int64_t j = 0; j < n; ++j) yr[j] += a[r] * brow[j];
+                }
+                open = 0;
+            }
+            if (end) break;
+            if (!open) {
+                memset(set, 0, sizeof set);
+                cur = c;
+                open = 1;
+            }
+            a[col[p] & 15] = val[p];
+            set[col[p] & 15] = 1;
+        }
+    }
+}
+
+/* Producer of that encoding (the reference ships the consumer only): per
+ * 16-row window, the window's entries ordered by (column, row), entries of
+ * equal (column, row) in CSR position order - the order in which ToBCSR's
+ * 16-way merge visits a window with sorted rows (custom_op.cpp:611-671), so
+ * every run of equal columns is one (16 x 1) block of csr_to_bcsr and the
+ * last duplicate wins in both.  Output: crow_window_ptr [nwin + 1] (entry
+ * offsets, = crow[min(16 w, nrows)]), unique_col_ids [nnz] holding
+ * (column << 4) | row, value [nnz]. */
+typedef struct { int64_t key, p; } cube_ent;
+
+static int cmp_cube_ent(const void *x, const void *y)
+{
+    const cube_ent *a = (const cube_ent *)x, *b = (const cube_ent *)y;
+    if (a->key != b->key) return a->key < b->key ? -1 : 1;
+    return a->p < b->p ? -1 : (a->p > b->p);
+}
+
+int orc_csr_to_spmm_cube(int64_t nrows, int64_t ncols, int64_t nnz, const int64_t *crow,
+                         const int64_t *col, const void *val, int64_t esz, int64_t window_size,
+                         orc_layout *out)
+{
+    memset(out, 0, sizeof *out);
+    if (window_size != 16) return fail("window_size must be 16");
+    if (check_csr(nrows, ncols, nnz, crow, col)) return 1;
+    const int64_t nwin = (nrows + 15) / 16;
+    out->crow_window_ptr = (int64_t *)xcalloc(nwin + 1, sizeof(int64_t));
+    out->unique_col_ids = (int64_t *)xcalloc(nnz, sizeof(int64_t));
+    out->value = (uint8_t *)xcalloc(nnz, esz);
+    cube_ent *e = (cube_ent *)xcalloc(nnz, sizeof(cube_ent));
+    if (!out->crow_window_ptr || !out->unique_col_ids || !out->value || !e) {
+        free(e);
+        orc_free_layout(out);
+        return fail("out of memory");
+    }
+    out->n_crow = nwin + 1;
+    out->n_uniq = out->n_value = nnz;
+    const uint8_t *v = (const uint8_t *)val;
+    for (int64_t w = 0; w <= nwin; ++w) out->crow_window_ptr[w] = crow[w * 16 < nrows ? w * 16 : nrows];
+    for (int64_t w = 0; w < nwin; ++w) {
+        const int64_t p0 = out->crow_window_ptr[w], p1 = out->crow_window_ptr[w + 1];
+        for (int64_t r = 16 * w; r < 16 * w + 16 && r < nrows; ++r)
+            for (int64_t p = crow[r]; p < crow[r + 1]; ++p) {
+                e[p].key = (col[p] << 4) | (r & 15);
+                e[p].p = p;
+            }
+        qsort(e + p0, (size_t)(p1 - p0), sizeof(cube_ent), cmp_cube_ent);
+        for (int64_t q = p0; q < p1; ++q) {
+            out->unique_col_ids[q] = e[q].key;
+            memcpy(out->value + q * esz, v + e[q].p * esz, (size_t)esz);
+        }
+    }
+    free(e);
+    return 0;
+}

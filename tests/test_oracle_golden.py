@@ -133,3 +133,68 @@ def test_make_start_matches_reference_rule():
     # chunk = 5 -> targets 0,5,10,15 -> rows 0,2,3,4 (searchsorted right - 1)
     assert s.tolist() == [0, 2, 3, 4]
     assert oracle.make_start(torch.zeros(3, dtype=torch.int64), 4).tolist() == [0, 0, 0, 0]
+
+
+def cube_to_bcsr(rowptr, col, value):
+    """(16 x 1)-block layout implied by a spmm_cube window encoding: runs of
+    equal column are blocks, the last entry of a row in a run wins."""
+    rp, c = rowptr.to(torch.int64).numpy(), col.to(torch.int64).numpy()
+    v = value.numpy()
+    cptr, ucol, vals = [0], [], []
+    for w in range(rp.size - 1):
+        last = None
+        for p in range(rp[w], rp[w + 1]):
+            cc, r = int(c[p]) >> 4, int(c[p]) & 15
+            if cc != last:
+                ucol.append(cc)
+                vals.append(np.zeros(16, v.dtype))
+                last = cc
+            vals[-1][r] = v[p]
+        cptr.append(len(ucol))
+    val = np.concatenate(vals) if vals else np.zeros(0, v.dtype)
+    return np.array(cptr, np.int64), np.array(ucol, np.int64), val
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_cube_producer_matches_reference_bcsr(name):
+    """Runs of the producer's window encoding are exactly the reference's
+    csr_to_bcsr blocks (golden, bit-exact), and the encoding keeps every
+    entry."""
+    z, nrows, ncols, crow, col, values, _ = load_case(name)
+    cube = oracle.csr_to_spmm_cube(crow, col, values, nrows, ncols, 16)
+    assert cube["rowptr"].dtype == crow.dtype and cube["col"].dtype == crow.dtype
+    assert cube["value"].dtype == values.dtype
+    assert cube["col"].numel() == col.numel()
+    nwin = (nrows + 15) // 16
+    assert torch.equal(cube["rowptr"].to(torch.int64),
+                       crow.to(torch.int64)[torch.clamp(torch.arange(nwin + 1) * 16, max=nrows)])
+    cptr, ucol, val = cube_to_bcsr(cube["rowptr"], cube["col"], cube["value"])
+    assert np.array_equal(cptr, z["csr_to_bcsr/crow_window_ptr"].astype(np.int64))
+    assert np.array_equal(ucol, z["csr_to_bcsr/unique_col_ids"].astype(np.int64))
+    assert np.array_equal(val.view(np.uint8), np.ascontiguousarray(z["csr_to_bcsr/value"]).view(np.uint8))
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_cube_semantics_reproduce_product(name):
+    z, nrows, ncols, crow, col, values, dense = load_case(name)
+    cube = oracle.csr_to_spmm_cube(crow, col, values, nrows, ncols, 16)
+    y = oracle.spmm_cube_f64(cube["rowptr"], cube["col"], cube["value"], dense)
+    assert y.shape == (16 * ((nrows + 15) // 16), dense.shape[1])
+    np.testing.assert_allclose(y[:nrows], z["spmm_f64"], rtol=1e-9, atol=1e-9)
+    assert not y[nrows:].any()
+
+
+def test_oracle_cube_runs_and_last_write():
+    """Hand-made window: a column that reappears after another column opens
+    a second block; a repeated row inside one run keeps the last value."""
+    B = torch.arange(4 * 16, dtype=torch.float64).reshape(4, 16) + 1
+    enc = lambda c, r: (c << 4) | r
+    rowptr = torch.tensor([0, 5, 5, 6])
+    col = torch.tensor([enc(1, 0), enc(1, 3), enc(1, 0), enc(2, 0), enc(1, 0), enc(3, 15)])
+    val = torch.tensor([5.0, 2.0, 7.0, 1.0, 3.0, 4.0])
+    y = oracle.spmm_cube_f64(rowptr, col, val, B)
+    want = np.zeros((48, 16))
+    want[0] = 7.0 * B[1] + 1.0 * B[2] + 3.0 * B[1]   # 5.0 overwritten by 7.0
+    want[3] = 2.0 * B[1]
+    want[32 + 15] = 4.0 * B[3]
+    np.testing.assert_array_equal(y, want)
