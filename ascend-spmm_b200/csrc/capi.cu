@@ -76,9 +76,9 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     if (misaligned(dense) || misaligned(out) || misaligned(workspace))
         return set_error(SPMM_ERR_ARG, "%s: dense, out and workspace must be 16-byte aligned", op);
     const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype);
-    if (workspace_bytes < plan.partial_bytes() || (plan.partial_bytes() && !workspace))
+    if (workspace_bytes < plan.workspace_bytes() || !workspace)
         return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
-                         workspace_bytes, plan.partial_bytes());
+                         workspace_bytes, plan.workspace_bytes());
     cudaError_t e;
     spmmb::DevStatus *st = spmmb::device_status_ptr(&e);
     if (!st) return cuda_error(e, op);
@@ -86,7 +86,7 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     a.rowptr = rowptr; a.col = col; a.val = value; a.B = dense; a.out = out;
     a.M = M; a.K = K; a.N = N; a.nnz = nnz; a.row_begin = 0;
     a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
-    a.partial = static_cast<float *>(workspace);
+    spmmb::set_workspace(a, plan, workspace);
     a.status = st;
     e = spmmb::launch_gather(a, itype, dtype, batch_depth, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, op);
@@ -95,7 +95,7 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
 
 size_t mixed_workspace(int64_t v_nnz, int64_t N, int dtype)
 {
-    return spmmb::plan_gather(v_nnz, N, dtype).partial_bytes();
+    return spmmb::plan_gather(v_nnz, N, dtype).workspace_bytes();
 }
 
 int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const void *Vrowptr,
@@ -139,7 +139,7 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
         a.rowptr = Vrowptr; a.col = Vcol; a.val = Vvalue; a.B = dense; a.out = out;
         a.M = v_rows; a.K = K; a.N = N; a.nnz = v_nnz; a.row_begin = 16 * n_windows;
         a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
-        a.partial = static_cast<float *>(workspace);
+        spmmb::set_workspace(a, plan, workspace);
         a.status = st;
         e = spmmb::launch_gather(a, itype, dtype, batch_depth, s);
         if (e != cudaSuccess) return cuda_error(e, op);
@@ -191,7 +191,7 @@ int spmm_device_status(int *code, int64_t *detail, int reset, void *stream)
 size_t spmm_csr_workspace_bytes(int64_t M, int64_t N, int64_t nnz, int dtype)
 {
     (void)M;
-    return spmmb::plan_gather(nnz, N, dtype).partial_bytes();
+    return spmmb::plan_gather(nnz, N, dtype).workspace_bytes();
 }
 
 int spmm_csr_launch(const void *rowptr, const void *col, const void *value, const void *dense,

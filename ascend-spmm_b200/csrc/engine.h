@@ -33,6 +33,10 @@ struct GatherPlan {
     int64_t nunits() const { return unit_end - unit_begin; }
     // fp32 head/tail partial rows, two per unit
     size_t partial_bytes() const { return (size_t)nunits() * 2 * (size_t)N * sizeof(float); }
+    // then the first row of every unit boundary (int64, nunits + 1 entries;
+    // used by the tensor-core kernel)
+    size_t rows_offset() const { return (partial_bytes() + 255) & ~size_t(255); }
+    size_t workspace_bytes() const { return rows_offset() + (size_t)(nunits() + 1) * sizeof(int64_t); }
 };
 
 GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype);
@@ -52,12 +56,28 @@ struct GatherArgs {
     int64_t unit_begin;
     int64_t unit_end;
     float *partial;     // (unit_end - unit_begin) * 2 * N floats
+    int64_t *unit_rows; // (unit_end - unit_begin) + 1 entries of scratch
     DevStatus *status;
 };
+
+// Points a's scratch arrays into a workspace of plan.workspace_bytes().
+inline void set_workspace(GatherArgs &a, const GatherPlan &plan, void *ws)
+{
+    a.partial = static_cast<float *>(ws);
+    a.unit_rows = ws ? reinterpret_cast<int64_t *>(static_cast<char *>(ws) + plan.rows_offset()) : nullptr;
+}
 
 // batch_depth: 0 = default gather batch, 1 = deeper batches (same sums).
 cudaError_t launch_gather(const GatherArgs &a, int itype, int dtype, int batch_depth,
                           cudaStream_t stream);
+
+// Tensor-core variant for fp16 rows of a multiple of 64 features
+// (gather_mma.cu); launch_gather picks it by default when eligible.  It may
+// coarsen the units (a is updated: the partial and unit_rows scratch of the
+// original plan is large enough); the caller then launches the fix-up of
+// split rows with the updated a.
+bool gather_mma_eligible(const GatherArgs &a, int dtype);
+cudaError_t launch_gather_mma(GatherArgs &a, int itype, int batch_depth, cudaStream_t stream);
 
 // ---- window path (window.cu) ----------------------------------------------
 

@@ -428,11 +428,6 @@ csr_stream_kernel(const GatherArgs a)
 // two batches stay in flight.  Row bookkeeping and the per-row fma order are
 // those of csr_stream_kernel, so results are bitwise identical.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem)
-{
-    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
-}
 __device__ __forceinline__ void cp_async16_cg_s(unsigned saddr, const void *gmem)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gmem) : "memory");
@@ -731,6 +726,16 @@ csr_fixup_kernel(const GatherArgs a)
     }
 }
 
+template <typename T, typename I>
+cudaError_t launch_fixup(const GatherArgs &a, cudaStream_t stream)
+{
+    const int64_t units = a.unit_end - a.unit_begin;
+    if (units <= 1) return cudaSuccess;
+    const int64_t fb = std::min<int64_t>((units + 7) / 8, 8LL * device_sm_count());
+    csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
 template <typename T, typename I, typename Kern>
 cudaError_t launch_kernel(Kern kern, const GatherArgs &a, int64_t units_per_warp, cudaStream_t stream)
 {
@@ -744,25 +749,22 @@ cudaError_t launch_kernel(Kern kern, const GatherArgs &a, int64_t units_per_warp
     blocks = std::max<int64_t>(blocks, 1);
     kern<<<(unsigned)blocks, kGatherThreads, 0, stream>>>(a);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    if (units > 1) {
-        const int64_t fb = std::min<int64_t>((units + 7) / 8, 8LL * device_sm_count());
-        csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
-        e = cudaGetLastError();
-    }
-    return e;
+    return e != cudaSuccess ? e : launch_fixup<T, I>(a, stream);
 }
 
-// Kernel choice for rows of >= 16 vectors (all produce identical sums; the
-// environment variable SPMM_B200_GATHER = ring | stream | row selects one for
-// A/B measurement).
+// Kernel choice.  Default: the tensor-core kernel where eligible (fp16,
+// N % 64 == 0), else the ring kernel for whole-warp rows, the stream kernel
+// for half-warp rows and the row kernel for narrower rows.  The environment
+// variable SPMM_B200_GATHER = ring | stream | row selects one of the CUDA-core
+// kernels (all three produce bitwise-identical sums) for A/B measurement.
 int gather_kernel_choice()
 {
     static const int choice = [] {
         const char *v = getenv("SPMM_B200_GATHER");
         if (v && strcmp(v, "row") == 0) return 2;
         if (v && strcmp(v, "stream") == 0) return 1;
-        return 0;
+        if (v && strcmp(v, "ring") == 0) return 0;
+        return -1;
     }();
     return choice;
 }
@@ -781,13 +783,7 @@ cudaError_t launch_ring(Kern kern, const GatherArgs &a, int units_per_warp, size
     blocks = std::max<int64_t>(1, std::min(blocks, (warps_needed + 7) / 8));
     kern<<<(unsigned)blocks, kGatherThreads, smem, stream>>>(a);
     e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    if (units > 1) {
-        const int64_t fb = std::min<int64_t>((units + 7) / 8, 8LL * device_sm_count());
-        csr_fixup_kernel<T, I><<<(unsigned)std::max<int64_t>(fb, 1), kGatherThreads, 0, stream>>>(a);
-        e = cudaGetLastError();
-    }
-    return e;
+    return e != cudaSuccess ? e : launch_fixup<T, I>(a, stream);
 }
 
 template <typename T, typename I, int G, int VPL, int U, int MINB>
@@ -796,7 +792,7 @@ cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
     if constexpr (G >= 16) {
         const int choice = gather_kernel_choice();
         const bool full = a.N / Vec<T>::kElems == G * VPL;
-        if (choice == 0 && a.K > 0 && G == 32) {
+        if (choice <= 0 && a.K > 0 && G == 32) {
             // ring (measured faster when a whole warp serves one row; half-warp
             // groups stay on the stream kernel): 2 * U positions x VPL
             // vectors per lane, 8 warps per block
@@ -823,6 +819,13 @@ cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
 template <typename T, typename I>
 cudaError_t launch_typed(const GatherArgs &a, int batch_depth, cudaStream_t s)
 {
+    if constexpr (sizeof(T) == 2) {
+        if (gather_kernel_choice() < 0 && gather_mma_eligible(a, SPMM_F16)) {
+            GatherArgs m = a;   // the tensor-core kernel may use coarser units
+            const cudaError_t e = launch_gather_mma(m, sizeof(I) == 4 ? SPMM_I32 : SPMM_I64, batch_depth, s);
+            return e != cudaSuccess ? e : launch_fixup<T, I>(m, s);
+        }
+    }
     const int64_t NV = a.N / Vec<T>::kElems;
     const bool deep = batch_depth != 0;
 #define SPMM_GATHER_CFG(G, VPL, U)                                                         \

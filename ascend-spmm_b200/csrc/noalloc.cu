@@ -9,7 +9,8 @@
 // stall other streams).  spmm_csr_launch needs a caller-provided workspace
 // of spmm_csr_workspace_bytes(); this variant needs none.
 //
-// How: the fp32 partial rows of the nnz-unit split (see gather.cu) live in
+// How: the fp32 partial rows of the nnz-unit split (see gather.cu) and the
+// per-unit first rows live in
 // g_noalloc_scratch below, a static __device__ array of kNoallocScratchBytes
 // (32 MiB) that every GPU loading this library holds until the process
 // exits.  Host code cannot use the array's name as a device address, so the
@@ -92,11 +93,11 @@ extern "C" int spmm_csr_launch_noalloc(const void *rowptr, const void *col, cons
         return capi_error(SPMM_ERR_ARG, "%s: dense and out must be 16-byte aligned", op);
 
     GatherPlan plan = plan_gather(nnz, N, dtype);
-    while (plan.partial_bytes() > kNoallocScratchBytes && plan.unit < kNoallocMaxUnit) {
+    while (plan.workspace_bytes() > kNoallocScratchBytes && plan.unit < kNoallocMaxUnit) {
         plan.unit *= 2;
         plan.unit_end = std::max<int64_t>(1, (nnz + plan.unit - 1) / plan.unit);
     }
-    if (plan.partial_bytes() > kNoallocScratchBytes)
+    if (plan.workspace_bytes() > kNoallocScratchBytes)
         return capi_error(SPMM_ERR_UNSUPPORTED,
                           "%s: %lld nonzeros at width %lld need more than the %zu-byte static scratch", op,
                           (long long)nnz, (long long)N, kNoallocScratchBytes);
@@ -109,7 +110,7 @@ extern "C" int spmm_csr_launch_noalloc(const void *rowptr, const void *col, cons
     a.rowptr = rowptr; a.col = col; a.val = value; a.B = dense; a.out = out;
     a.M = M; a.K = K; a.N = N; a.nnz = nnz; a.row_begin = 0;
     a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
-    a.partial = scratch;
+    set_workspace(a, plan, scratch);
     a.status = st;
     e = launch_gather(a, itype, dtype, 0, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return capi_error(SPMM_ERR_CUDA, "%s: %s", op, cudaGetErrorString(e));

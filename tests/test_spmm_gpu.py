@@ -278,11 +278,12 @@ torch.save(outs, sys.argv[2])
 """
 
 
-def test_stream_and_row_kernels_bitwise_identical(npu, tmp_path):
-    """The flat-stream kernel (mixed-precision fma.rn.f32.f16 / packed f32x2
-    fma) and the row kernel (convert + fmaf) produce the same bits for every
-    width and index type; the row kernel runs in a child process selected by
-    SPMM_B200_GATHER=row."""
+def test_cuda_core_kernels_bitwise_identical(npu, tmp_path):
+    """The CUDA-core kernels - ring (cp.async ring, mixed-precision
+    fma.rn.f32.f16 / packed f32x2 fma), flat stream and row (convert + fmaf) -
+    produce the same bits for every width and index type.  Each runs in a
+    child process selected by SPMM_B200_GATHER (the choice is read once per
+    process)."""
     import os
     import subprocess
     import sys
@@ -296,14 +297,23 @@ def test_stream_and_row_kernels_bitwise_identical(npu, tmp_path):
         val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
         B = torch.randn(900, N, generator=g).to(dtype)
         cases.append((crow, col, val, B))
-    ours = [csr_call(npu, *c).cpu() for c in cases]
-    src, dst = tmp_path / "in.pt", tmp_path / "out.pt"
+    src = tmp_path / "in.pt"
     torch.save(cases, src)
     here = os.path.dirname(os.path.abspath(__file__))
     paths = ":".join([os.path.join(here, "..", "ascend-spmm_b200"), here])
-    env = dict(os.environ, SPMM_B200_GATHER="row")
-    subprocess.run([sys.executable, "-c", _ROW_KERNEL_SNIPPET, str(src), str(dst), paths], env=env, check=True,
-                   timeout=300)
-    theirs = torch.load(dst)
-    for (c, a, b) in zip(cases, ours, theirs):
-        assert torch.equal(a, b), (c[3].shape, c[3].dtype)
+    results = {}
+    for kern in ("ring", "stream", "row"):
+        dst = tmp_path / f"out_{kern}.pt"
+        env = dict(os.environ, SPMM_B200_GATHER=kern)
+        subprocess.run([sys.executable, "-c", _ROW_KERNEL_SNIPPET, str(src), str(dst), paths], env=env, check=True,
+                       timeout=300)
+        results[kern] = torch.load(dst)
+    for kern in ("stream", "row"):
+        for (c, a, b) in zip(cases, results["ring"], results[kern]):
+            assert torch.equal(a, b), (kern, c[3].shape, c[3].dtype)
+    # the default (tensor-core kernel for fp16 widths that are multiples of
+    # 64) agrees with them within the reference tolerance
+    for c, r in zip(cases, results["ring"]):
+        y = csr_call(npu, *c).cpu()
+        assert_close(y, oracle.spmm_csr_f64(*c), c[3].dtype)
+        assert_close(r, oracle.spmm_csr_f64(*c), c[3].dtype)
