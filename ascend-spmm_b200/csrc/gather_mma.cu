@@ -546,8 +546,12 @@ cudaError_t launch_width(const GatherArgs &a, bool deep, cudaStream_t stream)
 
 bool gather_mma_eligible(const GatherArgs &a, int dtype)
 {
-    // column indices travel as 32-bit integers inside the kernel
-    return dtype == SPMM_F16 && a.K > 0 && a.K <= INT_MAX && a.N % 64 == 0 && a.N >= 64 && a.unit_rows != nullptr;
+    // Column indices travel as 32-bit integers inside the kernel.  Chosen
+    // for one 64- or 128-feature slice per row (measured faster than the
+    // CUDA-core ring kernel there); wider rows keep the ring kernel unless
+    // SPMM_B200_MMA names a variant.
+    const bool shape = dtype == SPMM_F16 && a.K > 0 && a.K <= INT_MAX && a.N % 64 == 0 && a.unit_rows != nullptr;
+    return shape && (a.N <= 128 || mma_variant() != 0);
 }
 
 cudaError_t launch_gather_mma(GatherArgs &a, int itype, int batch_depth, cudaStream_t stream)

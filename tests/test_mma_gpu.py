@@ -140,3 +140,20 @@ def test_mma_mixed_csr_part(npu):
     y = npu.spmm_ascend_cube(*[x.to(DEV) for x in args], B.to(DEV), start()[:20], start())
     torch.cuda.synchronize()
     assert_close(y[:700], oracle.spmm_csr_f64(crow, col, val, B), torch.float16, "mixed")
+
+
+def test_mma_forced_for_all_widths():
+    """Wider rows default to the CUDA-core ring kernel; rerun this module in a
+    child process with the tensor-core kernel forced for every width
+    (SPMM_B200_MMA, read once per process)."""
+    import os
+    import subprocess
+    import sys
+
+    if os.environ.get("SPMM_B200_MMA"):
+        pytest.skip("already running with a forced variant")
+    env = dict(os.environ, SPMM_B200_MMA="c128s3")
+    here = os.path.dirname(os.path.abspath(__file__))
+    r = subprocess.run([sys.executable, "-m", "pytest", "-x", "-q", "-p", "no:cacheprovider", os.path.abspath(__file__)],
+                       env=env, cwd=os.path.dirname(here), capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
