@@ -5,8 +5,9 @@ same operator.  A is cut into contiguous row ranges balanced by nonzeros at
 16-row window boundaries (so window layouts built per shard keep whole
 windows), B is replicated on every GPU, and each rank computes its own rows
 with the single-GPU operators - there is no communication in the SpMM
-itself.  C stays row-sharded; ``allgather_rows`` assembles the full C with one
-NCCL all-gather only when a caller asks for it.
+itself.  C stays row-sharded; ``allgather_rows`` assembles the full C over
+NCCL (one all-gather for equal shards, one broadcast per rank otherwise) only
+when a caller asks for it.
 """
 
 from __future__ import annotations
@@ -45,25 +46,33 @@ def shard_csr(rowptr, col, val, r0: int, r1: int):
     return rp.to(rowptr.dtype).contiguous(), col[p0:p1].contiguous(), val[p0:p1].contiguous()
 
 
-def allgather_rows(local: torch.Tensor, bounds: list[tuple[int, int]], group=None) -> torch.Tensor:
+def allgather_rows(local: torch.Tensor, bounds: list[tuple[int, int]], group=None, out=None) -> torch.Tensor:
     """Full C on every rank from row shards ``local`` ([r1 - r0, N] per rank).
 
-    Shards may be uneven: each is padded to the largest shard, gathered with
-    one all_gather_into_tensor (NCCL over NVLink on GPUs, gloo on CPU) and the
-    padding is dropped.
+    Equal shards: one all_gather_into_tensor straight into the result.
+    Uneven shards: the local shard is copied into its rows of the result and
+    every rank's rows are broadcast from their owner (NCCL over NVLink on
+    GPUs, gloo on CPU), so no padded copies are made: the result (or ``out``)
+    is the only extra buffer.
     """
     import torch.distributed as dist
 
     world = len(bounds)
     rows = [r1 - r0 for r0, r1 in bounds]
-    m = max(rows) if rows else 0
     tail = tuple(local.shape[1:])
-    padded = local.new_zeros((m, *tail))
-    padded[: local.shape[0]] = local
-    out = local.new_empty((world * m, *tail))
-    dist.all_gather_into_tensor(out, padded, group=group)
-    parts = [out[k * m: k * m + rows[k]] for k in range(world)]
-    return torch.cat(parts, 0)
+    total = sum(rows)
+    full = out if out is not None else local.new_empty((total, *tail))
+    if all(r == rows[0] for r in rows):
+        dist.all_gather_into_tensor(full, local.contiguous(), group=group)
+        return full
+    me = dist.get_rank(group) if group is not None else dist.get_rank()
+    offs = [sum(rows[:k]) for k in range(world)]
+    full[offs[me]: offs[me] + rows[me]].copy_(local)
+    for k in range(world):
+        if rows[k]:
+            src = dist.get_global_rank(group, k) if group is not None else k
+            dist.broadcast(full[offs[k]: offs[k] + rows[k]], src=src, group=group)
+    return full
 
 
 def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: bool = False, group=None):

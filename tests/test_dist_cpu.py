@@ -59,8 +59,12 @@ def _worker(rank, world, port, results):
         r0, r1 = bounds[rank]
         rp, c, v = shard_csr(w.rowptr, w.col, w.val, r0, r1)
         local = torch.from_numpy(oracle.spmm_csr_f64(rp, c, v, w.B))
-        full = allgather_rows(local, bounds)
-        results[rank] = full.numpy()
+        results[rank] = allgather_rows(local, bounds).numpy()           # uneven shards: broadcasts
+        half = w.M // 2 // 16 * 16
+        even = [(0, half), (half, 2 * half)]
+        rp, c, v = shard_csr(w.rowptr, w.col, w.val, *even[rank])
+        local = torch.from_numpy(oracle.spmm_csr_f64(rp, c, v, w.B))
+        results[("even", rank)] = allgather_rows(local, even).numpy()   # equal shards: all-gather
     finally:
         dist.destroy_process_group()
 
@@ -79,5 +83,8 @@ def test_allgather_reassembles_full_product():
             assert p.exitcode == 0
         w = workloads.make(3, scale=0.01)
         ref = oracle.spmm_csr_f64(w.rowptr, w.col, w.val, w.B)
+        half = w.M // 2 // 16 * 16
+        assert shard_bounds(w.rowptr, world)[0][1] != half   # the first case really is uneven
         for r in range(world):
             np.testing.assert_allclose(results[r], ref, rtol=0, atol=0)
+            np.testing.assert_allclose(results[("even", r)], ref[: 2 * half], rtol=0, atol=0)
