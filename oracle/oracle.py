@@ -22,6 +22,8 @@ Contents
   265-288, 782-875; op_kernel/spmm_cube.cpp:51-147) evaluated in float64 on the (already fp16/fp32-rounded)
   inputs - the same construction as the reference's unused
   ``cpu_reference`` (tests/aic_aiv_ablation/common.py:173-177).
+* ``neutronsparse_parts_np``: the NeutronSparse partition of the reference's
+  Table 6 helpers (tests/task_mapping/common.py:170-229) in NumPy.
 * ``cpu_reference``: that reference function restated (torch.sparse.mm in
   fp32), used as the timed CPU baseline of the reference's own CPU path.
 * ``make_start``: tests/task_mapping/common.py:119-127 restated.
@@ -334,6 +336,28 @@ def spmm_cube_f64(rowptr, col, value, dense) -> np.ndarray:
     return y
 
 
+def neutronsparse_parts_np(crow, col, rows, cols, assume_symmetric=False, threshold=None):
+    """tests/task_mapping/common.py:170-229 restated in NumPy (the
+    reference's own formulation): returns (window mask, window row counts,
+    CSR row counts, dense-row count, dense-column count)."""
+    indptr = _i64(crow)
+    columns = _i64(col)
+    row_degree = np.diff(indptr).astype(np.int64)
+    if assume_symmetric and rows == cols:
+        column_degree = row_degree.copy()
+    else:
+        column_degree = np.bincount(columns, minlength=cols).astype(np.int64)
+    edge_dense_column = (column_degree > threshold)[columns]
+    row_dense_degree = np.zeros(rows, dtype=np.int64)
+    nonempty = row_degree > 0
+    if nonempty.any():
+        row_dense_degree[nonempty] = np.add.reduceat(edge_dense_column, indptr[:-1][nonempty], dtype=np.int64)
+    dense_row = row_dense_degree > threshold
+    mask = np.logical_and(edge_dense_column, np.repeat(dense_row, row_degree))
+    cube_counts = np.where(dense_row, row_dense_degree, 0)
+    return mask, cube_counts, row_degree - cube_counts, int(dense_row.sum()), int((column_degree > threshold).sum())
+
+
 def cpu_reference(rows, cols, crow, col, values, dense) -> torch.Tensor:
     """tests/aic_aiv_ablation/common.py:173-177 restated: torch.sparse.mm in fp32."""
     matrix = torch.sparse_csr_tensor(crow, col, values.float(), size=(rows, cols),
@@ -359,5 +383,5 @@ def tolerance(dtype: torch.dtype) -> tuple[float, float]:
 
 __all__ = [
     "build", "csr_to_bcsr", "csr_to_ascend_cube", "block_level_split", "preprocess",
-    "csr_to_spmm_cube", "spmm_csr_f64", "spmm_mixed_f64", "spmm_cube_f64", "cpu_reference", "make_start", "tolerance",
+    "csr_to_spmm_cube", "spmm_csr_f64", "spmm_mixed_f64", "spmm_cube_f64", "neutronsparse_parts_np", "cpu_reference", "make_start", "tolerance",
 ]
