@@ -37,6 +37,33 @@ def _index(inv_permutation, device):
     return inv_permutation.to(device=device, dtype=torch.long).reshape(-1).contiguous()
 
 
+# Row scatter / gather on the GPU, differentiable like the reference's
+# index_copy_ / index_select (the gradient of one is the other).
+class _PackRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tensor, index, packed_rows):
+        ctx.save_for_backward(index)
+        return _pack_rows(tensor.contiguous(), index, packed_rows)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (index,) = ctx.saved_tensors
+        return _restore_rows(grad.contiguous(), index), None, None
+
+
+class _RestoreRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, packed, index):
+        ctx.save_for_backward(index)
+        ctx.rows = packed.size(0)
+        return _restore_rows(packed.contiguous(), index)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (index,) = ctx.saved_tensors
+        return _pack_rows(grad.contiguous(), index, ctx.rows), None
+
+
 def pack_node_tensor(tensor, inv_permutation, packed_rows=None):
     """Apply ``P`` once to a tensor whose leading dimension is original node id.
 
@@ -60,7 +87,7 @@ def pack_node_tensor(tensor, inv_permutation, packed_rows=None):
         packed_rows = int(packed_rows)
     if packed_rows < minimum_rows:
         raise ValueError("packed_rows is smaller than the permutation extent")
-    return _pack_rows(tensor.contiguous(), index, packed_rows)
+    return _PackRows.apply(tensor, index, packed_rows)
 
 
 def restore_node_tensor(packed_tensor, inv_permutation):
@@ -74,7 +101,7 @@ def restore_node_tensor(packed_tensor, inv_permutation):
         or int(index.max().item()) >= packed_tensor.size(0)
     ):
         raise ValueError("inv_permutation contains an invalid packed node id")
-    return _restore_rows(packed_tensor.contiguous(), index)
+    return _RestoreRows.apply(packed_tensor, index)
 
 
 __all__ = [
