@@ -22,6 +22,7 @@
 // STAGES = 1 is the unpipelined variant (the reference's SPTILE = 16
 // ablation, op_kernel/spmm_ascend_cube_aic_without_pipeline.cpp:6).
 #include <algorithm>
+#include <cstdlib>
 
 #include "../../include/spmm_b200.h"
 #include "common.cuh"
@@ -391,6 +392,8 @@ cudaError_t launch_f32(const WindowArgs &a, cudaStream_t stream)
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined, cudaStream_t stream)
 {
     if (a.nwin <= 0) return cudaSuccess;
+    if (pipelined && window_warp_eligible(a, dtype) && !getenv("SPMM_B200_WINDOW_BLOCK"))
+        return launch_window_warp(a, itype, stream);
     if (dtype == SPMM_F16) {
         if (itype == SPMM_I32) return pipelined ? launch_f16<int, 3>(a, stream) : launch_f16<int, 1>(a, stream);
         return pipelined ? launch_f16<int64_t, 3>(a, stream) : launch_f16<int64_t, 1>(a, stream);

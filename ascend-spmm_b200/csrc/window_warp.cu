@@ -1,0 +1,340 @@
+// Window path, warp-pipelined tensor-core kernel (fp16, N % 64 == 0).
+//
+// Same semantics as window.cu (reference: op_kernel/spmm_ascend_cube.cpp:
+// 52-165, 265-288, and the vector-core rows added on top, :782-875): window
+// slot s owns output rows [16s, 16s + 16) = sum over its (16 x 1) blocks of
+// Cvalue[16b + i] * B[Ccol[b], :] plus the CSR entries of those rows, summed
+// in fp32 and rounded once.
+//
+// Design: a warp owns (window, feature slice of FW = 64 or 128 features) and
+// runs on its own, no block-wide barrier.  The window's stream - its blocks,
+// then the CSR entries of its rows - is consumed in chunks of 16 entries:
+//  * gathers: the 16 B-row slices of a chunk go by 16-byte cp.async into the
+//    warp's STAGES-deep shared-memory ring together with the chunk's 16 x 16
+//    value tile (blocks) or its 16 values (CSR entries); the column indices
+//    of chunk x travel one pipeline depth earlier, in the copy group of chunk
+//    x - STAGES + 1, so no global load is ever waited on inside the loop;
+//  * math: D[feature, row] += sum_k Bg[k, feature] * V[k, row] with
+//    mma.sync m16n8k16, features as M (ldmatrix.trans of the staged rows),
+//    window rows as N in two halves of 8; for blocks the value tile is read
+//    with one ldmatrix.x4.trans, for CSR entries a value is placed at its
+//    row by comparing its position with the row ranges held in lanes;
+//  * epilogue: the 16 x FW fp32 tile is rounded to fp16 and written through
+//    a stmatrix.trans transpose as 16-byte row segments.
+#include <algorithm>
+#include <climits>
+
+#include "../../include/spmm_b200.h"
+#include "common.cuh"
+#include "engine.h"
+
+namespace spmmb {
+
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ void cp16(unsigned dst, const void *src, int bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void wait_groups() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void ldsm4t(unsigned addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void stsm4t(unsigned addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3)
+{
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(r0),
+                 "r"(r1), "r"(r2), "r"(r3)
+                 : "memory");
+}
+__device__ __forceinline__ void mma(float *d, const uint32_t *a, uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};\n"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t h2(float lo, float hi)
+{
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ unsigned lds16u(unsigned addr)
+{
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ int64_t lds_idx(unsigned addr, int isz)
+{
+    if (isz == 4) {
+        int v;
+        asm volatile("ld.shared.s32 %0, [%1];\n" : "=r"(v) : "r"(addr));
+        return v;
+    }
+    long long v;
+    asm volatile("ld.shared.s64 %0, [%1];\n" : "=l"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(unsigned addr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+
+template <int FW, int STAGES, int WARPS> struct WinShape {
+    static constexpr int kPitch = FW * 2 + 16;     // staged B row (16-byte pad: conflict-free ldmatrix)
+    static constexpr int kVPitch = 48;             // value-tile row: 16 values + pad (conflict-free ldmatrix)
+    static constexpr int kRows = 0;
+    static constexpr int kTile = kRows + 16 * kPitch;   // 16 x 16 value tile, or the values of 16 CSR entries
+    static constexpr int kCols = kTile + 16 * kVPitch;  // column indices of a later chunk (aligned copy)
+    static constexpr int kStage = kCols + 160;
+    static constexpr int kWarp = (STAGES * kStage + 16 * kPitch + 127) / 128 * 128;   // + 16-row epilogue tile
+    static constexpr int kBlock = WARPS * kWarp;
+};
+
+template <typename I, int FW, int STAGES, int WARPS, int MINB>
+__global__ void __launch_bounds__(WARPS * 32, MINB)
+window_warp_kernel(const WindowArgs a, int nslices)
+{
+    using L = WinShape<FW, STAGES, WARPS>;
+    constexpr int PITCH = L::kPitch;
+    constexpr int NMT = FW / 16;
+    constexpr int PIECES = FW / 8;
+    constexpr int ISZ = sizeof(I);
+    extern __shared__ __align__(128) unsigned char win_smem[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const unsigned base = (unsigned)__cvta_generic_to_shared(win_smem) + (unsigned)(wid * L::kWarp);
+    const unsigned epi = base + STAGES * L::kStage;
+
+    const I *cptr = static_cast<const I *>(a.cptr);
+    const I *ccol = static_cast<const I *>(a.ccol);
+    const char *cval = static_cast<const char *>(a.cval);
+    const I *vptr = static_cast<const I *>(a.vptr);
+    const I *vcol = static_cast<const I *>(a.vcol);
+    const char *vval = static_cast<const char *>(a.vval);
+    const char *B = static_cast<const char *>(a.B);
+    char *out = static_cast<char *>(a.out);
+    const int64_t rowbytes = a.N * 2;
+
+    const int64_t nitems = a.nwin * nslices;
+    for (int64_t it = (int64_t)blockIdx.x * WARPS + wid; it < nitems; it += (int64_t)gridDim.x * WARPS) {
+        const int64_t s = it / nslices;
+        const int f0 = (int)(it % nslices) * FW;
+
+        // ---- the window's stream: blocks [cb, cb + nb), CSR entries [vb, vb + nv)
+        int64_t cb = ld_idx(cptr + s), ce = ld_idx(cptr + s + 1);
+        if (cb < 0 || ce < cb || ce > a.nblocks) {
+            if (lane == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, s);
+            cb = ce = 0;
+        }
+        // lane r < 17 holds vptr[16 s + r] (rows past vrows are empty)
+        int64_t vr = 0;
+        if (a.vrows > 0 && 16 * s < a.vrows) vr = ld_idx(vptr + min(16 * s + min(lane, 16), a.vrows));
+        int64_t vb = __shfl_sync(kFull, vr, 0), ve = __shfl_sync(kFull, vr, 16);
+        {
+            const int64_t nxt = __shfl_down_sync(kFull, vr, 1);
+            const bool bad = (lane == 0 && (vb < 0 || ve > a.vnnz)) || (lane < 16 && nxt < vr);
+            if (__any_sync(kFull, bad)) {
+                if (lane == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, 16 * s);
+                vb = ve = 0;
+                vr = 0;
+            }
+        }
+        const int nb = (int)(ce - cb), nv = (int)(ve - vb);
+        const int nbc = (nb + 15) >> 4, nvc = (nv + 15) >> 4;
+        const int nch = nbc + nvc;
+        // row ranges of window rows g and 8 + g, relative to vb (CSR entries)
+        const int rb0 = (int)(__shfl_sync(kFull, vr, g) - vb), re0 = (int)(__shfl_sync(kFull, vr, g + 1) - vb);
+        const int rb1 = (int)(__shfl_sync(kFull, vr, g + 8) - vb), re1 = (int)(__shfl_sync(kFull, vr, g + 9) - vb);
+        const int misb = (int)((cb * ISZ) & 15), misv = (int)((vb * ISZ) & 15);   // column-array misalignment
+        const int misval = (int)((vb * 2) & 15);                                  // value-array misalignment
+
+        // Column indices of chunk x into the col slot of stage st: the
+        // aligned 16-byte pieces covering its 16 (or fewer) indices.
+        auto stage_cols = [&](int x, unsigned st) {
+            if (x >= nch) return;
+            const bool blk = x < nbc;
+            const char *arr = blk ? reinterpret_cast<const char *>(ccol) : reinterpret_cast<const char *>(vcol);
+            const int64_t first = blk ? cb + 16 * x : vb + 16 * (x - nbc);
+            const int64_t count = blk ? min(16, nb - 16 * x) : min(16, nv - 16 * (x - nbc));
+            const int64_t b0 = first * ISZ, b1 = (first + count) * ISZ;
+            const int64_t p0 = b0 & ~int64_t(15);
+            const int npieces = (int)((b1 - p0 + 15) >> 4);
+            if (lane < npieces) {
+                const int64_t pb = p0 + 16 * lane;
+                const int bytes = (int)max((int64_t)0, min((int64_t)16, b1 - pb));
+                cp16(st + L::kCols + 16 * lane, arr + (bytes > 0 ? pb : 0), bytes);
+            }
+        };
+        // Gathers (and values) of chunk x into stage st; its columns sit in
+        // that stage's col slot already.
+        auto stage_rows = [&](int x, unsigned st) {
+            if (x >= nch) return;
+            const bool blk = x < nbc;
+            const int k = lane & 15;
+            const int cnt = blk ? min(16, nb - 16 * x) : min(16, nv - 16 * (x - nbc));
+            const int mis = blk ? misb : misv;
+            int64_t c = -1;
+            if (k < cnt) {
+                c = lds_idx(st + L::kCols + mis + k * ISZ, ISZ);
+                if (c < 0 || c >= a.K) {
+                    if (lane < 16) raise_status(a.status, SPMM_DEV_BAD_COLUMN, s);
+                    c = -1;
+                }
+            }
+            const int cc = (int)c;
+            constexpr int RPI = 32 / PIECES;   // rows per instruction
+            const int v = lane % PIECES;
+#pragma unroll
+            for (int i = 0; i < 16 / RPI; ++i) {
+                const int kk = lane / PIECES + RPI * i;
+                const int ck = __shfl_sync(kFull, cc, kk);
+                const char *src = B + (int64_t)(ck >= 0 ? ck : 0) * rowbytes + f0 * 2 + v * 16;
+                cp16(st + (unsigned)(kk * PITCH + v * 16), src, ck >= 0 ? 16 : 0);
+            }
+            if (blk) {
+                // 16 blocks x 16 values, contiguous: lane -> half a block column
+                const int kk = lane >> 1, h = lane & 1;
+                const bool ok = kk < cnt;
+                const char *src = cval + ((cb + 16 * x + (ok ? kk : 0)) * 16 + 8 * h) * 2;
+                cp16(st + L::kTile + (unsigned)(kk * L::kVPitch + 16 * h), src, ok ? 16 : 0);
+            } else if (lane < 3) {
+                // the chunk's values: aligned pieces covering 16 fp16 entries
+                const int64_t b0 = (vb + 16 * (x - nbc)) * 2, b1 = b0 + 2 * cnt;
+                const int64_t pb = (b0 & ~int64_t(15)) + 16 * lane;
+                const int bytes = (int)max((int64_t)0, min((int64_t)16, b1 - pb));
+                cp16(st + L::kTile + 16 * lane, vval + (bytes > 0 ? pb : 0), bytes);
+            }
+        };
+        auto stage_of = [&](int x) -> unsigned { return base + (unsigned)((x % STAGES) * L::kStage); };
+
+        float acc0[NMT][4], acc1[NMT][4];
+#pragma unroll
+        for (int m = 0; m < NMT; ++m)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc0[m][e] = acc1[m][e] = 0.f;
+
+        // prologue: columns of chunks 0 .. STAGES-2, then their gathers (each
+        // group also carries the columns of the chunk STAGES-1 further on)
+#pragma unroll
+        for (int x = 0; x < STAGES - 1; ++x) stage_cols(x, stage_of(x));
+        commit();
+        wait_groups<0>();
+        __syncwarp();
+#pragma unroll
+        for (int x = 0; x < STAGES - 1; ++x) {
+            stage_rows(x, stage_of(x));
+            stage_cols(x + STAGES - 1, stage_of(x + STAGES - 1));
+            commit();
+        }
+
+        for (int c = 0; c < nch; ++c) {
+            wait_groups<STAGES - 2>();
+            __syncwarp();
+            // group c + STAGES - 1: gathers of that chunk (columns arrived with
+            // group c) and the columns of chunk c + 2 STAGES - 2
+            {
+                const int x = c + STAGES - 1;
+                stage_rows(x, stage_of(x));
+                stage_cols(x + STAGES - 1, stage_of(x + STAGES - 1));
+                commit();
+            }
+            const unsigned st = stage_of(c);
+            uint32_t bb[4];   // B operand: {b0, b1} for rows 0-7, then rows 8-15
+            if (c < nbc) {
+                const int tile = lane >> 3;
+                ldsm4t(st + L::kTile + (unsigned)(((tile & 1) * 8 + (lane & 7)) * L::kVPitch + (tile >> 1) * 16),
+                       bb[0], bb[1], bb[2], bb[3]);
+            } else {
+                const int q = 16 * (c - nbc) + 2 * t;   // positions q, q+1, q+8, q+9 (relative to vb)
+                const unsigned vs = st + L::kTile + (unsigned)misval;
+                const unsigned v0 = lds16u(vs + 2 * (2 * t)), v1 = lds16u(vs + 2 * (2 * t + 1));
+                const unsigned v2 = lds16u(vs + 2 * (2 * t + 8)), v3 = lds16u(vs + 2 * (2 * t + 9));
+                const unsigned w0 = (unsigned)(re0 - rb0), w1 = (unsigned)(re1 - rb1);
+                bb[0] = (((unsigned)(q - rb0) < w0) ? v0 : 0u) | ((((unsigned)(q + 1 - rb0) < w0) ? v1 : 0u) << 16);
+                bb[1] = (((unsigned)(q + 8 - rb0) < w0) ? v2 : 0u) | ((((unsigned)(q + 9 - rb0) < w0) ? v3 : 0u) << 16);
+                bb[2] = (((unsigned)(q - rb1) < w1) ? v0 : 0u) | ((((unsigned)(q + 1 - rb1) < w1) ? v1 : 0u) << 16);
+                bb[3] = (((unsigned)(q + 8 - rb1) < w1) ? v2 : 0u) | ((((unsigned)(q + 9 - rb1) < w1) ? v3 : 0u) << 16);
+            }
+#pragma unroll
+            for (int m = 0; m < NMT; ++m) {
+                const int tile = lane >> 3;
+                uint32_t af[4];
+                ldsm4t(st + (unsigned)(((tile >> 1) * 8 + (lane & 7)) * PITCH + (16 * m + 8 * (tile & 1)) * 2), af[0],
+                       af[1], af[2], af[3]);
+                mma(acc0[m], af, bb[0], bb[1]);
+                mma(acc1[m], af, bb[2], bb[3]);
+            }
+        }
+        wait_groups<0>();
+        __syncwarp();
+
+        // ---- epilogue: rows 16 s .. 16 s + 15, fp16, through the transpose tile
+#pragma unroll
+        for (int m = 0; m < NMT; m += 2) {
+            const int tile = lane >> 3;
+            const unsigned fo = (unsigned)((16 * (m + (tile >> 1)) + 8 * (tile & 1)) * 2);
+            stsm4t(epi + (unsigned)((lane & 7) * PITCH) + fo, h2(acc0[m][0], acc0[m][1]), h2(acc0[m][2], acc0[m][3]),
+                   h2(acc0[m + 1][0], acc0[m + 1][1]), h2(acc0[m + 1][2], acc0[m + 1][3]));
+            stsm4t(epi + (unsigned)((8 + (lane & 7)) * PITCH) + fo, h2(acc1[m][0], acc1[m][1]),
+                   h2(acc1[m][2], acc1[m][3]), h2(acc1[m + 1][0], acc1[m + 1][1]), h2(acc1[m + 1][2], acc1[m + 1][3]));
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < PIECES / 2; ++i) {
+            const int idx = lane + 32 * i;
+            const int n = idx / PIECES, v = idx % PIECES;
+            uint4 *o = reinterpret_cast<uint4 *>(out + (16 * s + n) * rowbytes + f0 * 2) + v;
+            __stcs(o, lds128(epi + (unsigned)(n * PITCH + v * 16)));
+        }
+        __syncwarp();
+    }
+}
+
+template <typename I, int FW, int STAGES, int WARPS>
+cudaError_t launch_ww(const WindowArgs &a, cudaStream_t stream)
+{
+    using L = WinShape<FW, STAGES, WARPS>;
+    constexpr int MINB = std::max(1, (220 * 1024) / L::kBlock);
+    auto kern = window_warp_kernel<I, FW, STAGES, WARPS, MINB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBlock);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, L::kBlock);
+    if (e != cudaSuccess) return e;
+    const int nslices = (int)(a.N / FW);
+    const int64_t items = a.nwin * nslices;
+    int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
+    blocks = std::max<int64_t>(1, std::min(blocks, (items + WARPS - 1) / WARPS));
+    kern<<<(unsigned)blocks, WARPS * 32, L::kBlock, stream>>>(a, nslices);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool window_warp_eligible(const WindowArgs &a, int dtype)
+{
+    // index and value arrays are copied in 16-byte pieces from 16-byte
+    // aligned bases; other layouts take the block-synchronous kernel
+    auto al = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    return dtype == SPMM_F16 && a.N % 64 == 0 && a.K > 0 && a.K <= INT_MAX && al(a.ccol) && al(a.cval) &&
+           al(a.vcol) && al(a.vval) && al(a.B) && al(a.out);
+}
+
+cudaError_t launch_window_warp(const WindowArgs &a, int itype, cudaStream_t stream)
+{
+    if (a.nwin <= 0) return cudaSuccess;
+    if (a.N % 128 == 0)
+        return itype == SPMM_I32 ? launch_ww<int, 128, 3, 4>(a, stream) : launch_ww<int64_t, 128, 3, 4>(a, stream);
+    return itype == SPMM_I32 ? launch_ww<int, 64, 3, 4>(a, stream) : launch_ww<int64_t, 64, 3, 4>(a, stream);
+}
+
+}  // namespace spmmb
