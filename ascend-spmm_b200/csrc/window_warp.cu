@@ -95,7 +95,10 @@ template <int FW, int STAGES, int WARPS> struct WinShape {
     static constexpr int kTile = kRows + 16 * kPitch;   // 16 x 16 value tile, or the values of 16 CSR entries
     static constexpr int kCols = kTile + 16 * kVPitch;  // column indices of a later chunk (aligned copy)
     static constexpr int kStage = kCols + 160;
-    static constexpr int kWarp = (STAGES * kStage + 16 * kPitch + 127) / 128 * 128;   // + 16-row epilogue tile
+    // The 16-row epilogue tile reuses the ring (it is written only after the
+    // last copy of the window has landed).
+    static_assert(16 * kPitch <= STAGES * kStage, "epilogue tile fits in the ring");
+    static constexpr int kWarp = (STAGES * kStage + 127) / 128 * 128;
     static constexpr int kBlock = WARPS * kWarp;
 };
 
@@ -112,7 +115,7 @@ window_warp_kernel(const WindowArgs a, int nslices)
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const unsigned base = (unsigned)__cvta_generic_to_shared(win_smem) + (unsigned)(wid * L::kWarp);
-    const unsigned epi = base + STAGES * L::kStage;
+    const unsigned epi = base;   // epilogue tile over the drained ring
 
     const I *cptr = static_cast<const I *>(a.cptr);
     const I *ccol = static_cast<const I *>(a.ccol);
