@@ -103,10 +103,11 @@ struct WindowArgs {
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined,
                           cudaStream_t stream);
 
-// Warp-pipelined tensor-core window kernel (window_warp.cu): fp16,
-// N % 64 == 0, 16-byte aligned arrays; launch_window uses it when eligible.
+// Warp-pipelined window kernels (window_warp.cu): fp16 N % 64 == 0 on
+// tensor cores, fp32 N % 128 == 0 on CUDA cores; 16-byte aligned arrays;
+// launch_window uses them when eligible.
 bool window_warp_eligible(const WindowArgs &a, int dtype);
-cudaError_t launch_window_warp(const WindowArgs &a, int itype, cudaStream_t stream);
+cudaError_t launch_window_warp(const WindowArgs &a, int itype, int dtype, cudaStream_t stream);
 
 // ---- spmm_cube (cube.cu) -----------------------------------------------------
 

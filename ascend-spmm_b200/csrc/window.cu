@@ -393,7 +393,7 @@ cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelin
 {
     if (a.nwin <= 0) return cudaSuccess;
     if (pipelined && window_warp_eligible(a, dtype) && !getenv("SPMM_B200_WINDOW_BLOCK"))
-        return launch_window_warp(a, itype, stream);
+        return launch_window_warp(a, itype, dtype, stream);
     if (dtype == SPMM_F16) {
         if (itype == SPMM_I32) return pipelined ? launch_f16<int, 3>(a, stream) : launch_f16<int, 1>(a, stream);
         return pipelined ? launch_f16<int64_t, 3>(a, stream) : launch_f16<int64_t, 1>(a, stream);

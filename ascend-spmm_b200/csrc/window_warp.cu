@@ -1,4 +1,5 @@
-// Window path, warp-pipelined tensor-core kernel (fp16, N % 64 == 0).
+// Window path, warp-pipelined kernels: tensor cores for fp16 (N % 64 == 0),
+// CUDA cores for fp32 (N % 128 == 0).
 //
 // Same semantics as window.cu (reference: op_kernel/spmm_ascend_cube.cpp:
 // 52-165, 265-288, and the vector-core rows added on top, :782-875): window
@@ -321,6 +322,245 @@ cudaError_t launch_ww(const WindowArgs &a, cudaStream_t stream)
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// fp32: same stream and pipeline, CUDA-core math.  Lane l owns features
+// f0 + 4 l .. f0 + 4 l + 3 of all 16 window rows (64 fp32 accumulators) and
+// multiplies with packed fma.rn.f32x2 (an IEEE fp32 fma per lane half; TF32
+// tensor cores would miss the 1e-4 tolerance).  A block updates all 16 rows
+// from its value column; a CSR entry updates only its row, chosen by a
+// warp-uniform switch.  Sums run over the window's blocks in order, then its
+// CSR entries in order.
+// ---------------------------------------------------------------------------
+template <int STAGES, int WARPS> struct WinShapeF32 {
+    static constexpr int kPitch = 512;             // 128 fp32 features per staged row
+    static constexpr int kTile = 16 * kPitch;      // 16 x 16 fp32 value tile (k-major), or 16 CSR values
+    static constexpr int kCols = kTile + 16 * 64 + 16;
+    static constexpr int kStage = kCols + 160;
+    static constexpr int kWarp = (STAGES * kStage + 127) / 128 * 128;
+    static constexpr int kBlock = WARPS * kWarp;
+};
+
+__device__ __forceinline__ void fma2(float &x, float &y, float v, float bx, float by)
+{
+    asm("{\n\t.reg .b64 a, vv, bb;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 vv, {%2, %2};\n\tmov.b64 bb, {%3, %4};\n\t"
+        "fma.rn.f32x2 a, vv, bb, a;\n\tmov.b64 {%0, %1}, a;\n\t}"
+        : "+f"(x), "+f"(y)
+        : "f"(v), "f"(bx), "f"(by));
+}
+__device__ __forceinline__ float4 lds_f4(unsigned addr)
+{
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ float lds_f(unsigned addr)
+{
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];\n" : "=f"(v) : "r"(addr));
+    return v;
+}
+
+template <typename I, int STAGES, int WARPS, int MINB>
+__global__ void __launch_bounds__(WARPS * 32, MINB)
+window_warp_f32_kernel(const WindowArgs a, int nslices)
+{
+    using L = WinShapeF32<STAGES, WARPS>;
+    constexpr int FW = 128;
+    constexpr int ISZ = sizeof(I);
+    extern __shared__ __align__(128) unsigned char win_smem[];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const unsigned base = (unsigned)__cvta_generic_to_shared(win_smem) + (unsigned)(wid * L::kWarp);
+
+    const I *cptr = static_cast<const I *>(a.cptr);
+    const I *ccol = static_cast<const I *>(a.ccol);
+    const char *cval = static_cast<const char *>(a.cval);
+    const I *vptr = static_cast<const I *>(a.vptr);
+    const I *vcol = static_cast<const I *>(a.vcol);
+    const char *vval = static_cast<const char *>(a.vval);
+    const char *B = static_cast<const char *>(a.B);
+    char *out = static_cast<char *>(a.out);
+    const int64_t rowbytes = a.N * 4;
+
+    const int64_t nitems = a.nwin * nslices;
+    for (int64_t it = (int64_t)blockIdx.x * WARPS + wid; it < nitems; it += (int64_t)gridDim.x * WARPS) {
+        const int64_t s = it / nslices;
+        const int f0 = (int)(it % nslices) * FW;
+
+        int64_t cb = ld_idx(cptr + s), ce = ld_idx(cptr + s + 1);
+        if (cb < 0 || ce < cb || ce > a.nblocks) {
+            if (lane == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, s);
+            cb = ce = 0;
+        }
+        int64_t vr = 0;
+        if (a.vrows > 0 && 16 * s < a.vrows) vr = ld_idx(vptr + min(16 * s + min(lane, 16), a.vrows));
+        int64_t vb = __shfl_sync(kFull, vr, 0), ve = __shfl_sync(kFull, vr, 16);
+        {
+            const int64_t nxt = __shfl_down_sync(kFull, vr, 1);
+            const bool bad = (lane == 0 && (vb < 0 || ve > a.vnnz)) || (lane < 16 && nxt < vr);
+            if (__any_sync(kFull, bad)) {
+                if (lane == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, 16 * s);
+                vb = ve = 0;
+                vr = 0;
+            }
+        }
+        const int nb = (int)(ce - cb), nv = (int)(ve - vb);
+        const int nbc = (nb + 15) >> 4, nvc = (nv + 15) >> 4;
+        const int nch = nbc + nvc;
+        // lane r < 16: end of window row r (relative to vb)
+        const int rend = (int)(__shfl_down_sync(kFull, vr, 1) - vb);
+        const int misb = (int)((cb * ISZ) & 15), misv = (int)((vb * ISZ) & 15);
+        const int misval = (int)((vb * 4) & 15);
+
+        auto stage_cols = [&](int x, unsigned st) {
+            if (x >= nch) return;
+            const bool blk = x < nbc;
+            const char *arr = blk ? reinterpret_cast<const char *>(ccol) : reinterpret_cast<const char *>(vcol);
+            const int64_t first = blk ? cb + 16 * x : vb + 16 * (x - nbc);
+            const int64_t count = blk ? min(16, nb - 16 * x) : min(16, nv - 16 * (x - nbc));
+            const int64_t b0 = first * ISZ, b1 = (first + count) * ISZ;
+            const int64_t p0 = b0 & ~int64_t(15);
+            const int npieces = (int)((b1 - p0 + 15) >> 4);
+            if (lane < npieces) {
+                const int64_t pb = p0 + 16 * lane;
+                const int bytes = (int)max((int64_t)0, min((int64_t)16, b1 - pb));
+                cp16(st + L::kCols + 16 * lane, arr + (bytes > 0 ? pb : 0), bytes);
+            }
+        };
+        auto stage_rows = [&](int x, unsigned st) {
+            if (x >= nch) return;
+            const bool blk = x < nbc;
+            const int cnt = blk ? min(16, nb - 16 * x) : min(16, nv - 16 * (x - nbc));
+            const int mis = blk ? misb : misv;
+            // column of row k held by lane k
+            int64_t c = -1;
+            if (lane < cnt) {
+                c = lds_idx(st + L::kCols + mis + lane * ISZ, ISZ);
+                if (c < 0 || c >= a.K) {
+                    raise_status(a.status, SPMM_DEV_BAD_COLUMN, s);
+                    c = -1;
+                }
+            }
+            const int cc = (int)c;
+            // 16 rows x 512 bytes: one row per instruction, lane -> 16-byte piece
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+                const int ck = __shfl_sync(kFull, cc, k);
+                const char *src = B + (int64_t)(ck >= 0 ? ck : 0) * rowbytes + f0 * 4 + lane * 16;
+                cp16(st + (unsigned)(k * L::kPitch + lane * 16), src, ck >= 0 ? 16 : 0);
+            }
+            if (blk) {
+                // 16 blocks x 16 fp32 values, contiguous: 64 pieces
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int piece = lane + 32 * h, kk = piece >> 2;
+                    const bool ok = kk < cnt;
+                    const char *src = cval + ((cb + 16 * x + (ok ? kk : 0)) * 16 + 4 * (piece & 3)) * 4;
+                    cp16(st + L::kTile + (unsigned)(piece * 16), src, ok ? 16 : 0);
+                }
+            } else if (lane < 5) {
+                const int64_t b0 = (vb + 16 * (x - nbc)) * 4, b1 = b0 + 4 * cnt;
+                const int64_t pb = (b0 & ~int64_t(15)) + 16 * lane;
+                const int bytes = (int)max((int64_t)0, min((int64_t)16, b1 - pb));
+                cp16(st + L::kTile + 16 * lane, vval + (bytes > 0 ? pb : 0), bytes);
+            }
+        };
+        auto stage_of = [&](int x) -> unsigned { return base + (unsigned)((x % STAGES) * L::kStage); };
+
+        float acc[16][4];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.f;
+
+#pragma unroll
+        for (int x = 0; x < STAGES - 1; ++x) stage_cols(x, stage_of(x));
+        commit();
+        wait_groups<0>();
+        __syncwarp();
+#pragma unroll
+        for (int x = 0; x < STAGES - 1; ++x) {
+            stage_rows(x, stage_of(x));
+            stage_cols(x + STAGES - 1, stage_of(x + STAGES - 1));
+            commit();
+        }
+
+        for (int c = 0; c < nch; ++c) {
+            wait_groups<STAGES - 2>();
+            __syncwarp();
+            {
+                const int x = c + STAGES - 1;
+                stage_rows(x, stage_of(x));
+                stage_cols(x + STAGES - 1, stage_of(x + STAGES - 1));
+                commit();
+            }
+            const unsigned st = stage_of(c);
+            if (c < nbc) {
+                const int cnt = min(16, nb - 16 * c);
+                for (int k = 0; k < cnt; ++k) {
+                    const float4 b = lds_f4(st + (unsigned)(k * L::kPitch + lane * 16));
+                    const unsigned vt = st + L::kTile + (unsigned)(k * 64);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 v = lds_f4(vt + 16 * q);
+                        const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            fma2(acc[4 * q + i][0], acc[4 * q + i][1], vv[i], b.x, b.y);
+                            fma2(acc[4 * q + i][2], acc[4 * q + i][3], vv[i], b.z, b.w);
+                        }
+                    }
+                }
+            } else {
+                const int p0 = 16 * (c - nbc);
+                const int cnt = min(16, nv - p0);
+                for (int k = 0; k < cnt; ++k) {
+                    const float4 b = lds_f4(st + (unsigned)(k * L::kPitch + lane * 16));
+                    const float v = lds_f(st + L::kTile + (unsigned)(misval + 4 * k));
+                    // row of position p0 + k: number of window rows ending at or before it
+                    const int row = __popc(__ballot_sync(kFull, lane < 16 && rend <= p0 + k));
+                    switch (row) {
+#define SPMM_ROW_CASE(R)                                  \
+    case R:                                               \
+        fma2(acc[R][0], acc[R][1], v, b.x, b.y);          \
+        fma2(acc[R][2], acc[R][3], v, b.z, b.w);          \
+        break;
+                        SPMM_ROW_CASE(0) SPMM_ROW_CASE(1) SPMM_ROW_CASE(2) SPMM_ROW_CASE(3)
+                        SPMM_ROW_CASE(4) SPMM_ROW_CASE(5) SPMM_ROW_CASE(6) SPMM_ROW_CASE(7)
+                        SPMM_ROW_CASE(8) SPMM_ROW_CASE(9) SPMM_ROW_CASE(10) SPMM_ROW_CASE(11)
+                        SPMM_ROW_CASE(12) SPMM_ROW_CASE(13) SPMM_ROW_CASE(14) SPMM_ROW_CASE(15)
+#undef SPMM_ROW_CASE
+                    default: break;
+                    }
+                }
+            }
+        }
+        wait_groups<0>();
+        __syncwarp();
+        // rows 16 s .. 16 s + 15: lane l stores its 16 bytes of each row
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+            __stcs(reinterpret_cast<float4 *>(out + (16 * s + r) * rowbytes + f0 * 4) + lane,
+                   make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]));
+    }
+}
+
+template <typename I, int STAGES, int WARPS>
+cudaError_t launch_ww_f32(const WindowArgs &a, cudaStream_t stream)
+{
+    using L = WinShapeF32<STAGES, WARPS>;
+    constexpr int MINB = std::max(1, (220 * 1024) / L::kBlock);
+    auto kern = window_warp_f32_kernel<I, STAGES, WARPS, MINB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBlock);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, L::kBlock);
+    if (e != cudaSuccess) return e;
+    const int nslices = (int)(a.N / 128);
+    const int64_t items = a.nwin * nslices;
+    int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
+    blocks = std::max<int64_t>(1, std::min(blocks, (items + WARPS - 1) / WARPS));
+    kern<<<(unsigned)blocks, WARPS * 32, L::kBlock, stream>>>(a, nslices);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool window_warp_eligible(const WindowArgs &a, int dtype)
@@ -328,13 +568,16 @@ bool window_warp_eligible(const WindowArgs &a, int dtype)
     // index and value arrays are copied in 16-byte pieces from 16-byte
     // aligned bases; other layouts take the block-synchronous kernel
     auto al = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
-    return dtype == SPMM_F16 && a.N % 64 == 0 && a.K > 0 && a.K <= INT_MAX && al(a.ccol) && al(a.cval) &&
-           al(a.vcol) && al(a.vval) && al(a.B) && al(a.out);
+    const bool width = dtype == SPMM_F16 ? a.N % 64 == 0 : (dtype == SPMM_F32 && a.N % 128 == 0);
+    return width && a.K > 0 && a.K <= INT_MAX && al(a.ccol) && al(a.cval) && al(a.vcol) && al(a.vval) && al(a.B) &&
+           al(a.out);
 }
 
-cudaError_t launch_window_warp(const WindowArgs &a, int itype, cudaStream_t stream)
+cudaError_t launch_window_warp(const WindowArgs &a, int itype, int dtype, cudaStream_t stream)
 {
     if (a.nwin <= 0) return cudaSuccess;
+    if (dtype == SPMM_F32)
+        return itype == SPMM_I32 ? launch_ww_f32<int, 3, 2>(a, stream) : launch_ww_f32<int64_t, 3, 2>(a, stream);
     if (a.N % 128 == 0)
         return itype == SPMM_I32 ? launch_ww<int, 128, 3, 4>(a, stream) : launch_ww<int64_t, 128, 3, 4>(a, stream);
     return itype == SPMM_I32 ? launch_ww<int, 64, 3, 4>(a, stream) : launch_ww<int64_t, 64, 3, 4>(a, stream);

@@ -181,7 +181,8 @@ def test_mixed_graph_layout_relabelled(npu):
 
 
 @pytest.mark.parametrize("dtype,N", [(torch.float16, 16), (torch.float16, 272), (torch.float16, 1024),
-                                     (torch.float32, 16), (torch.float32, 512)])
+                                     (torch.float16, 64), (torch.float32, 16), (torch.float32, 128),
+                                     (torch.float32, 384), (torch.float32, 512)])
 def test_mixed_random_windows(npu, dtype, N):
     """Windows with many blocks (several pipeline chunks), CSR rows fused into
     every window, and CSR rows beyond the window region."""
