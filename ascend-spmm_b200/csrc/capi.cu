@@ -289,6 +289,45 @@ int spmm_cube_launch(const void *rowptr, const void *col, const void *value, con
     return SPMM_OK;
 }
 
+size_t spmm_ascend_cube_tiles_workspace_bytes(int64_t n_windows, int64_t n_tiles, int64_t N, int itype, int dtype)
+{
+    (void)N;
+    if (n_windows <= 0) return 0;
+    return spmmb::tiles_workspace_bytes(n_windows, n_tiles, itype, dtype);
+}
+
+int spmm_ascend_cube_tiles_launch(const void *crow_window_ptr, const void *unique_col_ids, const void *value,
+                                  const void *dense, void *out, int64_t n_windows, int64_t n_tiles, int64_t K,
+                                  int64_t N, int itype, int dtype, void *workspace, size_t workspace_bytes,
+                                  void *stream)
+{
+    const char *op = "spmm_ascend_cube_tiles";
+    int rc = check_dense(dtype, N, 16, op);
+    if (rc) return rc;
+    if ((rc = check_itype(itype, op))) return rc;
+    if (n_windows < 0 || n_tiles < 0 || K < 0) return set_error(SPMM_ERR_ARG, "%s: negative size", op);
+    if (itype == SPMM_I32 && 16 * n_tiles > INT32_MAX)
+        return set_error(SPMM_ERR_ARG, "%s: 16 * %lld tiles do not fit int32 block offsets", op, (long long)n_tiles);
+    if (n_windows == 0) return SPMM_OK;
+    if (!crow_window_ptr || !dense || !out || (n_tiles > 0 && (!unique_col_ids || !value)))
+        return set_error(SPMM_ERR_ARG, "%s: null array", op);
+    if (misaligned(dense) || misaligned(out) || misaligned(workspace))
+        return set_error(SPMM_ERR_ARG, "%s: dense, out and workspace must be 16-byte aligned", op);
+    const size_t need = spmmb::tiles_workspace_bytes(n_windows, n_tiles, itype, dtype);
+    if (workspace_bytes < need || !workspace)
+        return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
+                         workspace_bytes, need);
+    cudaError_t e;
+    spmmb::DevStatus *st = spmmb::device_status_ptr(&e);
+    if (!st) return cuda_error(e, op);
+    spmmb::TileArgs a{};
+    a.tptr = crow_window_ptr; a.col = unique_col_ids; a.val = value; a.B = dense; a.out = out;
+    a.nwin = n_windows; a.ntiles = n_tiles; a.K = K; a.N = N; a.status = st;
+    e = spmmb::launch_tiles(a, itype, dtype, workspace, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_error(e, op);
+    return SPMM_OK;
+}
+
 int spmm_csr_to_spmm_cube_run(const void *crow, const void *col, const void *val, int64_t nrows, int64_t ncols,
                               int64_t nnz, int64_t window_size, int itype, int vbytes, const spmm_allocator *alloc,
                               spmm_layout *out, void *stream)

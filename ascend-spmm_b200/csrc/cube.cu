@@ -234,7 +234,96 @@ cudaError_t run_cube(const CubeArgs &a, const CubeWorkspace &ws, cudaStream_t s)
     return launch_window(w, sizeof(I) == 4 ? SPMM_I32 : SPMM_I64, sizeof(T) == 2 ? SPMM_F16 : SPMM_F32, 1, s);
 }
 
+// ---- 16 x 16 tiles of csr_to_ascend_cube -------------------------------------
+// The producer (custom_op.cpp:429-592) stores per window its distinct columns
+// in tiles of 16 (unique_col_ids[16 t + k], the last tile zero-padded) and
+// value[256 t + 16 r + k] = A[row r of the window, column k of tile t].  Tile
+// t is exactly blocks 16 t .. 16 t + 15 of the (16 x 1)-block stream with
+// each 16 x 16 value tile transposed, so the consumer transposes the tiles,
+// scales the window pointer by 16 and runs the window kernel with the
+// producer's column array as is.  Padding blocks (column 0, values 0) are
+// summed like any other block.
+
+struct TileWorkspace {
+    void *cptr;   // I [nwin + 1]
+    void *cval;   // T [256 * max(ntiles, 1)]
+    size_t bytes;
+};
+
+TileWorkspace carve_tiles(void *base, int64_t nwin, int64_t ntiles, int isz, int vsz)
+{
+    TileWorkspace w{};
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *p = base ? static_cast<char *>(base) + off : nullptr;
+        off += align256(bytes);
+        return static_cast<void *>(p);
+    };
+    w.cptr = take((size_t)isz * (size_t)(nwin + 1));
+    w.cval = take((size_t)vsz * 256 * (size_t)std::max<int64_t>(ntiles, 1));
+    w.bytes = off;
+    return w;
+}
+
+// One 256-thread CTA per tile (grid-stride): coalesced load of the tile,
+// transposed through shared memory, coalesced store.  CTA 0 also writes the
+// block pointer; a window pointer outside [0, ntiles] becomes -1, which the
+// window kernel reports as a malformed pointer.
+template <typename T, typename I>
+__global__ void __launch_bounds__(256)
+tiles_to_blocks_kernel(const I *tptr, const T *tval, int64_t nwin, int64_t ntiles, I *cptr, T *cval)
+{
+    __shared__ T s[16][17];
+    if (blockIdx.x == 0) {
+        for (int64_t w = threadIdx.x; w <= nwin; w += blockDim.x) {
+            const int64_t p = (int64_t)tptr[w];
+            cptr[w] = (p < 0 || p > ntiles) ? (I)-1 : (I)(16 * p);
+        }
+    }
+    const int r = threadIdx.x >> 4, k = threadIdx.x & 15;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        s[r][k] = tval[256 * t + threadIdx.x];                  // value[256 t + 16 r + k]
+        __syncthreads();
+        cval[256 * t + threadIdx.x] = s[k][r];                  // block 16 t + r, row k
+        __syncthreads();
+    }
+}
+
+template <typename T, typename I>
+cudaError_t run_tiles(const TileArgs &a, const TileWorkspace &ws, cudaStream_t s)
+{
+    const unsigned grid = (unsigned)std::max<int64_t>(
+        1, std::min<int64_t>(a.ntiles, (int64_t)device_sm_count() * 8));
+    tiles_to_blocks_kernel<T, I><<<grid, 256, 0, s>>>(static_cast<const I *>(a.tptr), static_cast<const T *>(a.val),
+                                                      a.nwin, a.ntiles, static_cast<I *>(ws.cptr),
+                                                      static_cast<T *>(ws.cval));
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    WindowArgs w{};
+    w.cptr = ws.cptr; w.ccol = a.col; w.cval = ws.cval;
+    w.vptr = nullptr; w.vcol = nullptr; w.vval = nullptr;
+    w.B = a.B; w.out = a.out;
+    w.nwin = a.nwin; w.nblocks = 16 * a.ntiles; w.vrows = 0; w.vnnz = 0;
+    w.K = a.K; w.N = a.N; w.status = a.status;
+    return launch_window(w, sizeof(I) == 4 ? SPMM_I32 : SPMM_I64, sizeof(T) == 2 ? SPMM_F16 : SPMM_F32, 1, s);
+}
+
 }  // namespace
+
+size_t tiles_workspace_bytes(int64_t nwin, int64_t ntiles, int itype, int dtype)
+{
+    return carve_tiles(nullptr, nwin, ntiles, itype == SPMM_I32 ? 4 : 8, dtype == SPMM_F16 ? 2 : 4).bytes;
+}
+
+cudaError_t launch_tiles(const TileArgs &a, int itype, int dtype, void *workspace, cudaStream_t stream)
+{
+    if (a.nwin <= 0) return cudaSuccess;
+    const TileWorkspace ws = carve_tiles(workspace, a.nwin, a.ntiles, itype == SPMM_I32 ? 4 : 8,
+                                         dtype == SPMM_F16 ? 2 : 4);
+    if (dtype == SPMM_F16)
+        return itype == SPMM_I32 ? run_tiles<__half, int>(a, ws, stream) : run_tiles<__half, int64_t>(a, ws, stream);
+    return itype == SPMM_I32 ? run_tiles<float, int>(a, ws, stream) : run_tiles<float, int64_t>(a, ws, stream);
+}
 
 size_t cube_workspace_bytes(int64_t nwin, int64_t nnz, int itype, int dtype)
 {

@@ -127,6 +127,23 @@ struct CubeArgs {
 size_t cube_workspace_bytes(int64_t nwin, int64_t nnz, int itype, int dtype);
 cudaError_t launch_cube(const CubeArgs &a, int itype, int dtype, void *workspace, cudaStream_t stream);
 
+// 16 x 16 tiles of csr_to_ascend_cube (cube.cu): tile t = blocks 16t..16t+15.
+struct TileArgs {
+    const void *tptr;    // [nwin + 1] tile offsets of each 16-row window
+    const void *col;     // [16 * ntiles] tile columns (last tile of a window zero-padded)
+    const void *val;     // [256 * ntiles] value[256 t + 16 row + k]
+    const void *B;
+    void *out;           // [16 * nwin, N]
+    int64_t nwin;
+    int64_t ntiles;
+    int64_t K;
+    int64_t N;
+    DevStatus *status;
+};
+
+size_t tiles_workspace_bytes(int64_t nwin, int64_t ntiles, int itype, int dtype);
+cudaError_t launch_tiles(const TileArgs &a, int itype, int dtype, void *workspace, cudaStream_t stream);
+
 // ---- row permutation copies (rows.cu) ---------------------------------------
 
 cudaError_t launch_pack_rows(const void *src, const int64_t *inv, int64_t n, int64_t row_bytes, void *dst,

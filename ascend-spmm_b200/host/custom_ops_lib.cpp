@@ -283,6 +283,47 @@ at::Tensor spmm_cube_impl(const at::Tensor &rowptr, const at::Tensor &col, const
 }
 
 // ---------------------------------------------------------------------------
+// spmm_ascend_cube_tiles: consumer of csr_to_ascend_cube's 16 x 16 tiles
+// (custom_op.cpp:429-592 is the producer; the reference has no consumer).
+// Same checks and messages as spmm_cube; output [16 * windows, N].
+// ---------------------------------------------------------------------------
+at::Tensor spmm_ascend_cube_tiles_impl(const at::Tensor &crow_window_ptr, const at::Tensor &unique_col_ids,
+                                       const at::Tensor &value, const at::Tensor &dense)
+{
+    const char *op = "spmm_ascend_cube_tiles";
+    TORCH_CHECK_CUDA(crow_window_ptr);
+    TORCH_CHECK_CUDA(unique_col_ids);
+    TORCH_CHECK_CUDA(value);
+    TORCH_CHECK_CUDA(dense);
+    TORCH_CHECK(crow_window_ptr.dim() == 1, "row must be a 1D Tensor, but got: ", crow_window_ptr.dim());
+    TORCH_CHECK(unique_col_ids.dim() == 1, "col must be a 1D Tensor, but got: ", unique_col_ids.dim());
+    TORCH_CHECK(value.dim() == 1, "value must be a 1D Tensor, but got: ", value.dim());
+    TORCH_CHECK(dense.dim() == 2, "dense must be a 2D Tensor, but got: ", dense.dim());
+    check_dense_contract(dense, 16, op);
+    check_value_contract(value, dense, "value");
+    TORCH_CHECK(unique_col_ids.size(0) % 16 == 0, op, ": unique_col_ids must hold 16 columns per tile, but got ",
+                unique_col_ids.size(0));
+    TORCH_CHECK(value.size(0) == 16 * unique_col_ids.size(0), op,
+                ": value must hold 256 entries per tile, but got ", value.size(0), " for ",
+                unique_col_ids.size(0) / 16, " tiles");
+    TORCH_CHECK(crow_window_ptr.size(0) >= 1, op, ": crow_window_ptr must hold windows + 1 entries");
+    same_device({&crow_window_ptr, &unique_col_ids, &value}, dense, op);
+    const int itype = index_code({&crow_window_ptr, &unique_col_ids}, op);
+    c10::cuda::CUDAGuard guard(dense.device());
+
+    const int64_t nwin = crow_window_ptr.size(0) - 1, D = dense.size(1), ntiles = unique_col_ids.size(0) / 16;
+    at::Tensor result = at::empty({nwin * 16, D}, dense.options());
+    const int dt = dtype_code(dense);
+    const size_t wbytes = spmm_ascend_cube_tiles_workspace_bytes(nwin, ntiles, D, itype, dt);
+    at::Tensor ws = workspace(wbytes, dense);
+    const at::Tensor B = aligned16(dense);
+    check_rc(spmm_ascend_cube_tiles_launch(crow_window_ptr.data_ptr(), unique_col_ids.data_ptr(), value.data_ptr(),
+                                           B.data_ptr(), result.data_ptr(), nwin, ntiles, dense.size(0), D, itype, dt,
+                                           ws.data_ptr(), wbytes, stream_of(dense)));
+    return result;
+}
+
+// ---------------------------------------------------------------------------
 // Layout builders: csr_to_bcsr, csr_to_ascend_cube, block_level_split,
 // preprocess (custom_op.cpp:429-1412).  Same argument order and dict keys as
 // the reference; inputs may be CPU or CUDA tensors (CPU inputs are copied to
@@ -544,6 +585,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m)
     m.def("spmm_cube", &spmm_cube_impl,
           "CUDA window SpMM over (column << 4 | row) entries; width divisible by 16, MAXD=1024 for FP16 and 512 "
           "for FP32");
+    m.def("spmm_ascend_cube_tiles", &spmm_ascend_cube_tiles_impl,
+          "CUDA SpMM over csr_to_ascend_cube's 16 x 16 tiles (crow_window_ptr, unique_col_ids, value, dense); "
+          "width divisible by 16, MAXD=1024 for FP16 and 512 for FP32");
     m.def("spmm_ascend_cube", &spmm_ascend_cube_impl,
           "CUDA mixed window/CSR SpMM; width divisible by 16, MAXD=1024 for FP16 and 512 for FP32");
     m.def("spmm_ascend_cube_aic_without_pipeline", &spmm_ascend_cube_aic_without_pipeline_impl,

@@ -18,6 +18,7 @@ from custom_ops_lib import (  # noqa: F401  (re-exported API)
     spmm_ascend_cube,
     spmm_ascend_cube_aic_without_pipeline,
     spmm_ascend_cube_aiv_mb,
+    spmm_ascend_cube_tiles,
     spmm_csr,
     spmm_csr_aiv_mb_batch,
     spmm_cube,
@@ -115,6 +116,7 @@ __all__ = [
     "spmm_ascend_cube",
     "spmm_ascend_cube_aic_without_pipeline",
     "spmm_ascend_cube_aiv_mb",
+    "spmm_ascend_cube_tiles",
     "spmm_csr",
     "spmm_csr_aiv_mb_batch",
     "spmm_cube",

@@ -62,7 +62,7 @@ def parse_args():
     p.add_argument("--scale", type=float, default=1.0)
     p.add_argument("--op", choices=("csr", "mixed"), default="csr")
     p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
-    p.add_argument("--e2e-steps", type=int, default=8)
+    p.add_argument("--e2e-steps", type=int, default=24)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--gather", action="store_true",

@@ -165,6 +165,20 @@ int spmm_cube_launch(const void *rowptr, const void *col, const void *value, con
                      int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
                      size_t workspace_bytes, void *stream);
 
+/* Consumer of csr_to_ascend_cube's 16 x 16 tiles (custom_op.cpp:429-592;
+ * the reference ships the producer only).  crow_window_ptr [n_windows + 1]
+ * in tiles, unique_col_ids [16 * n_tiles], value [256 * n_tiles] with
+ * value[256 t + 16 row + k]; output [16 * n_windows, N], rows in original
+ * order.  Padding columns of a window's last tile (column 0, values 0) are
+ * summed like any other entry.  N % 16 == 0 for fp16 and fp32; with int32
+ * indices 16 * n_tiles must fit in int32. */
+size_t spmm_ascend_cube_tiles_workspace_bytes(int64_t n_windows, int64_t n_tiles, int64_t N, int itype,
+                                              int dtype);
+int spmm_ascend_cube_tiles_launch(const void *crow_window_ptr, const void *unique_col_ids, const void *value,
+                                  const void *dense, void *out, int64_t n_windows, int64_t n_tiles, int64_t K,
+                                  int64_t N, int itype, int dtype, void *workspace, size_t workspace_bytes,
+                                  void *stream);
+
 /* ---------------------------------------------------------------------- */
 /* Layout builders (GPU, bit-exact with the reference's CPU preprocessing). */
 /* Inputs: CSR on the device (crow [nrows + 1], col [nnz], val [nnz] with  */

@@ -336,6 +336,22 @@ def spmm_cube_f64(rowptr, col, value, dense) -> np.ndarray:
     return y
 
 
+def spmm_ascend_cube_tiles_f64(crow_window_ptr, unique_col_ids, value, dense) -> np.ndarray:
+    """SpMM over the 16 x 16 tiles of ``csr_to_ascend_cube`` in float64
+    ([16 * #windows, N]): y[16 w + r] = sum over the window's tiles t and
+    k < 16 of value[256 t + 16 r + k] * B[unique_col_ids[16 t + k]]
+    (tile layout of custom_op.cpp:429-592; padding entries are literal
+    zeros of column 0)."""
+    tp, c, v, B = _i64(crow_window_ptr), _i64(unique_col_ids), _f64(value), _f64(dense)
+    nwin, n = tp.size - 1, B.shape[1]
+    y = np.zeros((16 * nwin, n), np.float64)
+    for w in range(nwin):
+        for t in range(int(tp[w]), int(tp[w + 1])):
+            tile = v[256 * t: 256 * t + 256].reshape(16, 16)        # [row, k]
+            y[16 * w: 16 * w + 16] += tile @ B[c[16 * t: 16 * t + 16]]
+    return y
+
+
 def neutronsparse_parts_np(crow, col, rows, cols, assume_symmetric=False, threshold=None):
     """tests/task_mapping/common.py:170-229 restated in NumPy (the
     reference's own formulation): returns (window mask, window row counts,
@@ -383,5 +399,5 @@ def tolerance(dtype: torch.dtype) -> tuple[float, float]:
 
 __all__ = [
     "build", "csr_to_bcsr", "csr_to_ascend_cube", "block_level_split", "preprocess",
-    "csr_to_spmm_cube", "spmm_csr_f64", "spmm_mixed_f64", "spmm_cube_f64", "neutronsparse_parts_np", "cpu_reference", "make_start", "tolerance",
+    "csr_to_spmm_cube", "spmm_csr_f64", "spmm_mixed_f64", "spmm_cube_f64", "spmm_ascend_cube_tiles_f64", "neutronsparse_parts_np", "cpu_reference", "make_start", "tolerance",
 ]

@@ -181,3 +181,101 @@ def test_spmm_cube_invalid_column_is_reported(npu):
     assert code == 1   # SPMM_DEV_BAD_COLUMN
     assert torch.allclose(y[2].float().cpu(), B[1].float(), atol=1e-3)
     assert not bool(y[3].any())
+
+
+# ---- spmm_ascend_cube_tiles: consumer of csr_to_ascend_cube's 16 x 16 tiles ----
+
+def tiles_call(npu, t, B):
+    return npu.spmm_ascend_cube_tiles(t["crow_window_ptr"].to(DEV), t["unique_col_ids"].to(DEV),
+                                      t["value"].to(DEV), B.to(DEV))
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_tiles_on_golden_layouts(npu, name):
+    """GPU producer (bit-exact with the golden csr_to_ascend_cube) feeding the
+    tile consumer reproduces A @ B and the literal tile semantics."""
+    c = load_golden(name)
+    nrows, ncols = c["nrows"], c["ncols"]
+    t = npu.csr_to_ascend_cube(c["crow"].to(DEV), c["col"].to(DEV), c["values"].to(DEV), nrows, ncols, 16)
+    y = tiles_call(npu, t, c["dense"])
+    torch.cuda.synchronize()
+    assert y.shape == (16 * ((nrows + 15) // 16), c["dense"].shape[1]) and y.dtype == c["values"].dtype
+    assert_close(y[:nrows], c["z"]["spmm_f64"], y.dtype, name)
+    assert not bool(y[nrows:].any())
+    ref = oracle.spmm_ascend_cube_tiles_f64(t["crow_window_ptr"].cpu(), t["unique_col_ids"].cpu(),
+                                            t["value"].cpu(), c["dense"])
+    assert_close(y, ref, y.dtype, name + " tiles")
+    check_status(npu)
+
+
+@pytest.mark.parametrize("dtype,N", [(torch.float16, 16), (torch.float16, 128), (torch.float16, 1024),
+                                     (torch.float32, 16), (torch.float32, 128), (torch.float32, 512)])
+@pytest.mark.parametrize("idt", [torch.int32, torch.int64])
+def test_tiles_random_widths(npu, dtype, N, idt):
+    M, K = 533, 401
+    crow, col = rand_csr(M, K, 0.05, seed=N + 11, long_rows={7: 390, 530: 200}, empty_every=13, idt=idt)
+    g = torch.Generator().manual_seed(N + 1)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
+    B = torch.randn(K, N, generator=g).to(dtype)
+    t = npu.csr_to_ascend_cube(crow.to(DEV), col.to(DEV), val.to(DEV), M, K, 16)
+    y = tiles_call(npu, t, B)
+    assert_close(y[:M], oracle.spmm_csr_f64(crow, col, val, B), dtype, f"{dtype} N={N} {idt}")
+    if dtype == torch.float32:
+        np.testing.assert_allclose(y.cpu().double().numpy()[:M], oracle.spmm_csr_f64(crow, col, val, B),
+                                   rtol=1e-4, atol=1e-4)
+    check_status(npu)
+
+
+def test_tiles_hand_made_layout(npu):
+    """Tiles written by hand, not by the producer: repeated columns across
+    tiles, a window with no tiles, and entries in the padding positions."""
+    g = torch.Generator().manual_seed(21)
+    K, N = 50, 32
+    tptr = torch.tensor([0, 2, 2, 5], dtype=torch.int64)
+    ucol = torch.randint(0, K, (16 * 5,), generator=g, dtype=torch.int64)
+    val = (torch.rand(256 * 5, generator=g) * 2 - 1).half()
+    B = torch.randn(K, N, generator=g).half()
+    for idt in (torch.int32, torch.int64):
+        t = {"crow_window_ptr": tptr.to(idt), "unique_col_ids": ucol.to(idt), "value": val}
+        y = tiles_call(npu, t, B)
+        assert_close(y, oracle.spmm_ascend_cube_tiles_f64(tptr, ucol, val, B), torch.float16, str(idt))
+        assert not bool(y[16:32].any())
+    check_status(npu)
+
+
+def test_tiles_config3_sample(npu):
+    w = workloads.make(3, scale=0.02)
+    t = npu.csr_to_ascend_cube(w.rowptr.to(DEV), w.col.to(DEV), w.val.to(DEV), w.M, w.K, 16)
+    y = tiles_call(npu, t, w.B)
+    assert_close(y[: w.M], oracle.spmm_csr_f64(w.rowptr, w.col, w.val, w.B), torch.float16, "cfg3 tiles")
+    check_status(npu)
+
+
+def test_tiles_edges_and_contract(npu):
+    B = torch.randn(10, 16).half()
+    empty = {"crow_window_ptr": torch.zeros(1, dtype=torch.int32), "unique_col_ids": torch.zeros(0, dtype=torch.int32),
+             "value": torch.zeros(0).half()}
+    assert tiles_call(npu, empty, B).shape == (0, 16)
+    no_tiles = dict(empty, crow_window_ptr=torch.zeros(3, dtype=torch.int32))
+    y = tiles_call(npu, no_tiles, B)
+    assert y.shape == (32, 16) and not bool(y.any())
+    one = {"crow_window_ptr": torch.tensor([0, 1], dtype=torch.int32),
+           "unique_col_ids": torch.zeros(16, dtype=torch.int32), "value": torch.zeros(256).half()}
+    with pytest.raises(RuntimeError, match="requires feature width divisible by 16, but got 8"):
+        tiles_call(npu, one, torch.randn(5, 8).half())
+    with pytest.raises(RuntimeError, match="value must hold 256 entries per tile"):
+        tiles_call(npu, dict(one, value=torch.zeros(255).half()), B)
+    with pytest.raises(RuntimeError, match="unique_col_ids must hold 16 columns per tile"):
+        tiles_call(npu, dict(one, unique_col_ids=torch.zeros(15, dtype=torch.int32)), B)
+    with pytest.raises(RuntimeError, match="value must have the same dtype as dense"):
+        tiles_call(npu, dict(one, value=torch.zeros(256)), B)
+    check_status(npu)
+
+
+def test_tiles_bad_window_pointer_is_reported(npu):
+    t = {"crow_window_ptr": torch.tensor([0, 3], dtype=torch.int32),    # 3 > 1 tile
+         "unique_col_ids": torch.zeros(16, dtype=torch.int32), "value": torch.ones(256).half()}
+    tiles_call(npu, t, torch.randn(4, 16).half())
+    torch.cuda.synchronize()
+    code, _ = npu.device_status(True)
+    assert code == 2   # SPMM_DEV_BAD_ROWPTR

@@ -198,3 +198,17 @@ def test_oracle_cube_runs_and_last_write():
     want[3] = 2.0 * B[1]
     want[32 + 15] = 4.0 * B[3]
     np.testing.assert_array_equal(y, want)
+
+
+@pytest.mark.parametrize("name", [c[0] for c in CASES])
+def test_oracle_tile_semantics_reproduce_product(name):
+    """The reference's own csr_to_ascend_cube tiles (golden fixtures), read
+    as value[256 t + 16 r + k] x B[unique_col_ids[16 t + k]], give A @ B:
+    the semantics the tile consumer implements."""
+    z, nrows, _, _, _, _, dense = load_case(name)
+    t = {k.split("/", 1)[1]: torch.from_numpy(np.ascontiguousarray(z[k]))
+         for k in z.files if k.startswith("csr_to_ascend_cube/")}
+    y = oracle.spmm_ascend_cube_tiles_f64(t["crow_window_ptr"], t["unique_col_ids"], t["value"], dense)
+    assert y.shape == (16 * ((nrows + 15) // 16), dense.shape[1])
+    np.testing.assert_allclose(y[:nrows], z["spmm_f64"], rtol=1e-9, atol=1e-9)
+    assert not y[nrows:].any()
