@@ -421,12 +421,21 @@ csr_stream_kernel(const GatherArgs a)
 // Ring kernel: the stream kernel with its gathers landing in shared memory.
 //
 // Each lane copies the 16-byte pieces of the B rows it will itself consume
-// (cp.async.cg, L2 only) into a per-group ring of 2 x U positions and reads
+// (cp.async.cg, L2 only) into a per-warp ring of 2 x U positions and reads
 // them back with one 16-byte shared load per position: no cross-lane
 // synchronisation is needed (cp.async.wait_group covers the thread's own
-// copies), in-flight data holds no registers, so more groups fit per SM and
-// two batches stay in flight.  Row bookkeeping and the per-row fma order are
-// those of csr_stream_kernel, so results are bitwise identical.
+// copies), in-flight data holds no registers, so more warps fit per SM and
+// two batches stay in flight.  Column indices and values are staged per
+// 64-nonzero chunk in the warp's shared memory (two chunks resident, the
+// next one in registers), so a batch reads its U columns and U values with
+// a few broadcast vector loads instead of per-position register selects and
+// shuffles; a batch with no row end inside skips the per-position row tests.
+// Row ends are found warp-parallel: a rolling window holds the unit-local
+// end positions of the next 32-64 rows (one lane per row, prefetched 32 rows
+// ahead), one ballot per batch yields the batch's row-end mask and each
+// ending row's index goes to a per-warp shared table; a batch that the
+// current row spans skips this step.  The per-row fma order is that of
+// csr_stream_kernel, so results are bitwise identical.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async16_cg_s(unsigned saddr, const void *gmem)
 {
@@ -441,28 +450,114 @@ __device__ __forceinline__ uint4 lds16(unsigned saddr)
 __device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 
+// Shared memory of one warp in the ring kernel: the ring (2 batches of U
+// positions x VPL 16-byte pieces per lane), then two staged chunks of 64
+// column indices and 64 values.
+template <typename T, int VPL, int U> struct RingShape {
+    static constexpr int kChunk = 64;
+    static constexpr int kRingBytes = 2 * U * VPL * 32 * 16;
+    static constexpr int kColOff = kRingBytes;
+    static constexpr int kValOff = kColOff + 2 * kChunk * 4;
+    static constexpr int kRowOff = kValOff + 2 * kChunk * (int)sizeof(typename FmaVec<T>::Scalar);
+    // a multiple of 128 bytes, so each 512-byte ring position starts on a
+    // 128-byte boundary (4 shared-memory wavefronts per warp access, not 5)
+    static constexpr int kWarpBytes = (kRowOff + 2 * U * 8 + 127) / 128 * 128;
+};
+
+// fp16 products of one nonzero (half SEL of the packed value word) with the
+// 8 elements of a 16-byte B piece, accumulated in fp32.
+__device__ __forceinline__ void fma8_f16_lo(float *acc, unsigned vw, const uint4 &b)
+{
+    asm("{\n\t.reg .f16 s, t, l0, u0, l1, u1, l2, u2, l3, u3;\n\t"
+        "mov.b32 {s, t}, %8;\n\t"
+        "mov.b32 {l0, u0}, %9;\n\tmov.b32 {l1, u1}, %10;\n\tmov.b32 {l2, u2}, %11;\n\tmov.b32 {l3, u3}, %12;\n\t"
+        "fma.rn.f32.f16 %0, s, l0, %0;\n\tfma.rn.f32.f16 %1, s, u0, %1;\n\t"
+        "fma.rn.f32.f16 %2, s, l1, %2;\n\tfma.rn.f32.f16 %3, s, u1, %3;\n\t"
+        "fma.rn.f32.f16 %4, s, l2, %4;\n\tfma.rn.f32.f16 %5, s, u2, %5;\n\t"
+        "fma.rn.f32.f16 %6, s, l3, %6;\n\tfma.rn.f32.f16 %7, s, u3, %7;\n\t}"
+        : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+          "+f"(acc[7])
+        : "r"(vw), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+}
+__device__ __forceinline__ void fma8_f16_hi(float *acc, unsigned vw, const uint4 &b)
+{
+    asm("{\n\t.reg .f16 s, t, l0, u0, l1, u1, l2, u2, l3, u3;\n\t"
+        "mov.b32 {t, s}, %8;\n\t"
+        "mov.b32 {l0, u0}, %9;\n\tmov.b32 {l1, u1}, %10;\n\tmov.b32 {l2, u2}, %11;\n\tmov.b32 {l3, u3}, %12;\n\t"
+        "fma.rn.f32.f16 %0, s, l0, %0;\n\tfma.rn.f32.f16 %1, s, u0, %1;\n\t"
+        "fma.rn.f32.f16 %2, s, l1, %2;\n\tfma.rn.f32.f16 %3, s, u1, %3;\n\t"
+        "fma.rn.f32.f16 %4, s, l2, %4;\n\tfma.rn.f32.f16 %5, s, u2, %5;\n\t"
+        "fma.rn.f32.f16 %6, s, l3, %6;\n\tfma.rn.f32.f16 %7, s, u3, %7;\n\t}"
+        : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+          "+f"(acc[7])
+        : "r"(vw), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w));
+}
+
+// Product of nonzero j of a batch (its value packed in the words vw) with one
+// 16-byte B piece; j is a compile-time constant after unrolling.
+template <typename T> struct BatchFma;
+template <> struct BatchFma<__half> {
+    template <int NW>
+    static __device__ __forceinline__ void run(float *acc, const unsigned (&vw)[NW], int j, const uint4 &b)
+    {
+        if (j & 1) fma8_f16_hi(acc, vw[j >> 1], b);
+        else fma8_f16_lo(acc, vw[j >> 1], b);
+    }
+};
+template <> struct BatchFma<float> {
+    template <int NW>
+    static __device__ __forceinline__ void run(float *acc, const unsigned (&vw)[NW], int j, const uint4 &b)
+    {
+        FmaVec<float>::run(acc, __uint_as_float(vw[j]), b);
+    }
+};
+
+// NW consecutive 32-bit words from shared memory with the widest loads the
+// alignment allows (callers keep 4 * NW-byte alignment); every lane reads the
+// same address, so each load is a broadcast.
+template <int NW>
+__device__ __forceinline__ void lds_words(const void *p, unsigned (&w)[NW])
+{
+    if constexpr (NW % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NW / 4; ++i) {
+            const uint4 x = reinterpret_cast<const uint4 *>(p)[i];
+            w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+        }
+    } else if constexpr (NW == 2) {
+        const uint2 x = *reinterpret_cast<const uint2 *>(p);
+        w[0] = x.x; w[1] = x.y;
+    } else {
+        static_assert(NW == 1, "1, 2 or a multiple of 4 words");
+        w[0] = *reinterpret_cast<const unsigned *>(p);
+    }
+}
+
 template <typename T, typename I, int G, int VPL, int U, int MINB, bool FULL>
 __global__ void __launch_bounds__(kGatherThreads, MINB)
 csr_ring_kernel(const GatherArgs a)
 {
-    static_assert(G == 16 || G == 32, "ring groups are half-warps or warps");
+    static_assert(G == 32, "the ring serves whole-warp rows");
     using F = FmaVec<T>;
     using Scalar = typename F::Scalar;
-    constexpr int S = 32 / G;
+    using Shape = RingShape<T, VPL, U>;
     constexpr int EPV = Vec<T>::kElems;
-    constexpr int CH = 64;          // nonzeros per prefetched column/value chunk
-    constexpr int PER = CH / G;
-    constexpr int RING = 2 * U;     // positions in the ring (two batches)
-    static_assert(CH % U == 0 && U <= G, "batches tile the chunk");
+    constexpr int CH = Shape::kChunk;   // nonzeros per staged column/value chunk
+    constexpr int PER = CH / 32;
+    constexpr int VB = (int)sizeof(Scalar);
+    static_assert(CH % U == 0 && 2 * U <= CH && (U * VB) % 4 == 0 && U <= 32, "batches tile the chunk");
     extern __shared__ __align__(16) uint4 ring_smem[];
     const int lane = threadIdx.x & 31;
-    const int sub = lane / G, gl = lane % G, shift = sub * G;
-    const unsigned gmask = (G == 32) ? 0xffffffffu : (((1u << G) - 1u) << shift);
-    const int group_in_block = (threadIdx.x >> 5) * S + sub;
+    const int gl = lane;
+    constexpr unsigned gmask = 0xffffffffu;
+    char *wbase = reinterpret_cast<char *>(ring_smem) + (size_t)(threadIdx.x >> 5) * Shape::kWarpBytes;
     // this lane's column of the ring, as a 32-bit shared address
-    const unsigned ring_s = (unsigned)__cvta_generic_to_shared(ring_smem + (size_t)group_in_block * RING * VPL * G + gl);
-    const int64_t stream = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * S + sub;
-    const int64_t nstreams = (((int64_t)gridDim.x * blockDim.x) >> 5) * S;
+    const unsigned ring_s = (unsigned)__cvta_generic_to_shared(wbase) + (unsigned)lane * 16;
+    int *s_col = reinterpret_cast<int *>(wbase + Shape::kColOff);            // [2][CH], chunk n in slot n & 1
+    Scalar *s_val = reinterpret_cast<Scalar *>(wbase + Shape::kValOff);      // [2][CH]
+    int64_t *s_row = reinterpret_cast<int64_t *>(wbase + Shape::kRowOff);    // [2][U] row ending at each position
+    const int64_t stream = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nstreams = ((int64_t)gridDim.x * blockDim.x) >> 5;
 
     const I *rowptr = static_cast<const I *>(a.rowptr);
     const I *col = static_cast<const I *>(a.col);
@@ -475,25 +570,10 @@ csr_ring_kernel(const GatherArgs a)
         const int64_t lo = u * a.unit;
         const int64_t hi = min(lo + a.unit, a.nnz);
         const bool last = (u == a.unit_end - 1);
-        const int64_t i0 = group_lower_bound<I, G>(rowptr, a.row_begin, a.M + 1, lo, gmask, gl, shift);
+        const int64_t i0 = group_lower_bound<I, G>(rowptr, a.row_begin, a.M + 1, lo, gmask, gl, 0);
         int64_t r = i0;
         if (i0 > a.row_begin && (i0 > a.M || ld_idx(rowptr + i0) > lo)) r = i0 - 1;
 
-        int64_t rc = r;
-        int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
-        int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
-        auto rp = [&](int64_t x) -> int64_t {
-            if (x < rc || x >= rc + 2 * G) {
-                rc = x;
-                rpa = ld_idx(rowptr + min(rc + gl, a.M));
-                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
-            } else if (x >= rc + G) {
-                rc += G;
-                rpa = rpb;
-                rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
-            }
-            return __shfl_sync(gmask, rpa, (int)(x - rc), G);
-        };
         auto zero_row = [&](int64_t row) {
 #pragma unroll
             for (int q = 0; q < VPL; ++q) {
@@ -501,24 +581,79 @@ csr_ring_kernel(const GatherArgs a)
                 if (FULL || vi < NV) __stcs(out + row * NV + vi, make_uint4(0, 0, 0, 0));
             }
         };
-
+        // first row with a nonzero in the unit; the empty rows before it that
+        // start inside the unit are written as zeros
         int64_t beg = 0, end = 0;
         bool have_row = false;
-        for (; r < a.M; ++r) {
-            beg = rp(r);
-            end = rp(r + 1);
-            if (beg < 0 || end < beg || end > a.nnz) {
-                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
-                break;
+        {
+            int64_t rc = r;
+            int64_t rpa = ld_idx(rowptr + min(rc + gl, a.M));
+            int64_t rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+            auto rp = [&](int64_t x) -> int64_t {
+                if (x < rc || x >= rc + 2 * G) {
+                    rc = x;
+                    rpa = ld_idx(rowptr + min(rc + gl, a.M));
+                    rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+                } else if (x >= rc + G) {
+                    rc += G;
+                    rpa = rpb;
+                    rpb = ld_idx(rowptr + min(rc + G + gl, a.M));
+                }
+                return __shfl_sync(gmask, rpa, (int)(x - rc), G);
+            };
+            for (; r < a.M; ++r) {
+                beg = rp(r);
+                end = rp(r + 1);
+                if (beg < 0 || end < beg || end > a.nnz) {
+                    if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
+                    break;
+                }
+                if (beg >= hi && !last) break;
+                if (end > beg) { have_row = true; break; }
+                zero_row(r);
             }
-            if (beg >= hi && !last) break;
-            if (end > beg) { have_row = true; break; }
-            zero_row(r);
         }
         if (!have_row) continue;
         const int64_t s0 = max(lo, beg);
-        bool head_pending = beg < lo;
-        const int nbatch = (int)((hi - s0 + U - 1) / U);
+        bool head_pending = beg < lo;   // the first segment is a head partial
+        const int H = (int)(hi - s0);   // positions of the unit, local to s0
+        const int nbatch = (H + U - 1) / U;
+
+        // Row ends as unit-local positions: lane l of a window based at row w
+        // holds rowptr[w + l + 1] - s0 (H + 1 past the unit, INT_MAX past M).
+        // A = rows [w0, w0 + 32), B = the next 32, C = the 32 after (raw,
+        // loaded 32 rows before it is needed).  rcur = first unfinished row.
+        bool bad = false;
+        auto load_raw = [&](int64_t w) -> int64_t { return ld_idx(rowptr + min(w + gl + 1, a.M)); };
+        auto conv = [&](int64_t raw, int64_t w, int before) -> int {
+            const int64_t row = w + gl;
+            int le;
+            bool wrong = false;
+            if (row >= a.M) {
+                le = INT_MAX;
+            } else {
+                wrong = raw > a.nnz || raw < s0;
+                le = raw > hi ? H + 1 : (int)(raw - s0);
+            }
+            const int pl = __shfl_up_sync(gmask, le, 1);
+            wrong = wrong || le < (gl ? pl : before);
+            if (__any_sync(gmask, wrong)) {
+                if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, w);
+                bad = true;
+            }
+            return wrong ? INT_MAX : le;
+        };
+        int64_t w0 = r, rcur = r;
+        int winA, winB;
+        int64_t rawC;
+        {
+            const int64_t ra = load_raw(w0), rb = load_raw(w0 + 32);
+            rawC = load_raw(w0 + 64);
+            winA = conv(ra, w0, -1);
+            winB = conv(rb, w0 + 32, __shfl_sync(gmask, winA, 31));
+        }
+        int carry = -1;   // local end of row rcur - 1
+        int cur_le = __shfl_sync(gmask, winA, 0);   // local end of row rcur
 
         float acc[VPL][EPV];
 #pragma unroll
@@ -526,9 +661,8 @@ csr_ring_kernel(const GatherArgs a)
 #pragma unroll
             for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
 
-        // column/value chunks: A holds chunk ka, B chunk ka + 1
-        int colA[PER], colB[PER];
-        Scalar valA[PER], valB[PER];
+        // Invalid columns become column 0 with value 0 (this kernel runs only
+        // with K > 0), so the gather needs no predicate beyond the batch end.
         auto load_chunk = [&](int64_t pos, int *cc, Scalar *vv) {
 #pragma unroll
             for (int k = 0; k < PER; ++k) {
@@ -546,45 +680,53 @@ csr_ring_kernel(const GatherArgs a)
                 }
             }
         };
-        int ka = 0;
-        load_chunk(s0, colA, valA);
-        load_chunk(s0 + CH, colB, valB);
-        // Entry o (offset from s0) lives in chunk o / CH (A = chunk ka,
-        // B = chunk ka + 1), register slot (o % CH) / G, lane o % G.  A batch
-        // never straddles a slot (U divides G), so the register is chosen once
-        // per batch and each entry costs one shuffle.
-        auto pick_col = [&](int o0) -> int {
-            const bool inA = (o0 / CH) == ka;
-            const int slot = (o0 % CH) / G;
-            int cw = inA ? colA[0] : colB[0];
+        auto stage = [&](int slot, const int *cc, const Scalar *vv) {
 #pragma unroll
-            for (int k = 1; k < PER; ++k)
-                if (slot == k) cw = inA ? colA[k] : colB[k];
-            return cw;
+            for (int k = 0; k < PER; ++k) {
+                s_col[slot * CH + gl + k * G] = cc[k];
+                s_val[slot * CH + gl + k * G] = vv[k];
+            }
         };
-        auto pick_val = [&](int o0) -> Scalar {
-            const bool inA = (o0 / CH) == ka;
-            const int slot = (o0 % CH) / G;
-            Scalar vw = inA ? valA[0] : valB[0];
-#pragma unroll
-            for (int k = 1; k < PER; ++k)
-                if (slot == k) vw = inA ? valA[k] : valB[k];
-            return vw;
-        };
+        // chunks 0 and 1 staged in shared memory, chunk 2 in registers
+        int colR[PER];
+        Scalar valR[PER];
+        __syncwarp();   // the previous unit's reads of the staging slots are done
+        {
+            int c0[PER];
+            Scalar v0[PER];
+            load_chunk(s0, c0, v0);
+            load_chunk(s0 + CH, colR, valR);
+            stage(0, c0, v0);
+            stage(1, colR, valR);
+            load_chunk(s0 + 2 * CH, colR, valR);
+        }
+        __syncwarp();
+
         auto issue = [&](int k) {
             if (k < nbatch) {
                 const int o0 = k * U;
-                const int nv = (int)min((int64_t)U, hi - (s0 + o0));
-                const int cw = pick_col(o0);
+                const int nv = min(U, H - o0);
+                unsigned cw[U];
+                lds_words<U>(s_col + ((o0 / CH) & 1) * CH + (o0 % CH), cw);
                 const unsigned slot0 = ring_s + (unsigned)((k & 1) * U * VPL * G * 16);
+                if (nv == U) {
 #pragma unroll
-                for (int j = 0; j < U; ++j) {
-                    const int c = __shfl_sync(gmask, cw, (o0 + j) % G, G);
-                    if (j < nv) {
-                        const uint4 *src = Bl + (int64_t)c * NV;
+                    for (int j = 0; j < U; ++j) {
+                        const uint4 *src = Bl + (int64_t)(int)cw[j] * NV;
 #pragma unroll
                         for (int q = 0; q < VPL; ++q)
                             if (FULL || gl + q * G < NV) cp_async16_cg_s(slot0 + (j * VPL + q) * G * 16, src + q * G);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < U; ++j) {
+                        if (j < nv) {
+                            const uint4 *src = Bl + (int64_t)(int)cw[j] * NV;
+#pragma unroll
+                            for (int q = 0; q < VPL; ++q)
+                                if (FULL || gl + q * G < NV)
+                                    cp_async16_cg_s(slot0 + (j * VPL + q) * G * 16, src + q * G);
+                        }
                     }
                 }
             }
@@ -593,97 +735,119 @@ csr_ring_kernel(const GatherArgs a)
         issue(0);
         issue(1);
 
-        bool done = false;
-        for (int k = 0; k < nbatch && !done; ++k) {
-            const int64_t pbase = s0 + (int64_t)k * U;
-            const int nvalid = (int)min((int64_t)U, hi - pbase);
-            const int64_t bend = pbase + nvalid;
-            // row bookkeeping of this batch (as in csr_stream_kernel)
+        for (int k = 0; k < nbatch && !bad; ++k) {
+            const int o0 = k * U;
+            const int nvalid = min(U, H - o0);
+            const int lim = o0 + nvalid;
+            const int buf = k & 1;
+            // Rows ending in this batch, warp-parallel over the window: their
+            // end positions form the mask `ends`, s_row[buf][j] names the row
+            // ending at position o0 + j; empty rows among them are zeroed.
+            // Empty rows starting at hi belong to the next unit (unless last).
             unsigned ends = 0, tails = 0;
-            int64_t myrow = 0;
-            for (;;) {
-                if (end <= bend) {
-                    const int jb = (int)(end - pbase - 1);
-                    ends |= 1u << jb;
-                    if (gl == jb) myrow = r;
-                    const int64_t prev = end;
-                    bool next = false;
-                    for (++r; r < a.M; ++r) {
-                        beg = prev;
-                        end = rp(r + 1);
-                        if (end < beg || end > a.nnz) {
-                            if (gl == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, r);
-                            break;
-                        }
-                        if (beg >= hi && !last) break;
-                        if (end > beg) { next = true; break; }
-                        zero_row(r);
-                    }
-                    if (!next) { done = true; break; }
-                    continue;
+            const bool any_end = cur_le <= lim;
+            if (any_end) __syncwarp();   // earlier reads of s_row[buf] are done
+            for (; cur_le <= lim;) {   // some row ends in this batch
+                const int d = (int)(rcur - w0);
+                const int src = (d + gl) & 31;
+                const int va = __shfl_sync(gmask, winA, src);
+                const int vb = __shfl_sync(gmask, winB, src);
+                const int le = (d + gl < 32) ? va : vb;
+                const int up = __shfl_up_sync(gmask, le, 1);
+                const bool empty = le == (gl ? up : carry);
+                const bool in = le <= lim && (last || !empty || le < H);
+                const int nin = __popc(__ballot_sync(gmask, in));
+                const int pos = le - 1 - o0;   // in [0, nvalid) for every row ending here
+                const bool endhere = in && !empty && (unsigned)pos < (unsigned)U;
+                ends |= __reduce_or_sync(gmask, endhere ? 1u << pos : 0u);
+                if (endhere) s_row[buf * U + pos] = rcur + gl;
+                unsigned em = __ballot_sync(gmask, in && empty);
+                while (em) {
+                    const int b = __ffs(em) - 1;
+                    em &= em - 1;
+                    zero_row(rcur + b);
                 }
-                if (bend == hi) {
-                    ends |= 1u << (nvalid - 1);
-                    tails |= 1u << (nvalid - 1);
-                    if (gl == nvalid - 1) myrow = r;
-                    done = true;
+                if (nin) carry = __shfl_sync(gmask, le, nin - 1);
+                cur_le = __shfl_sync(gmask, le, nin & 31);   // row rcur + nin (re-read below when nin == 32)
+                rcur += nin;
+                if (rcur - w0 >= 32) {
+                    winA = winB;
+                    winB = conv(rawC, w0 + 64, __shfl_sync(gmask, winB, 31));
+                    w0 += 32;
+                    rawC = load_raw(w0 + 64);
                 }
-                break;
+                if (nin < 32 || bad) break;
+                cur_le = __shfl_sync(gmask, (int)(rcur - w0) < 32 ? winA : winB, (int)(rcur - w0) & 31);
             }
+            if (lim == H && !((ends >> (nvalid - 1)) & 1u)) {   // a row continues past the unit
+                ends |= 1u << (nvalid - 1);
+                tails |= 1u << (nvalid - 1);
+            }
+            unsigned vw[U * VB / 4];
+            lds_words<U * VB / 4>(s_val + ((o0 / CH) & 1) * CH + (o0 % CH), vw);
+            if (any_end) __syncwarp();   // s_row entries of this batch are visible
             cp_async_wait_1();   // this lane's copies of batch k have landed
             const unsigned slot0 = ring_s + (unsigned)((k & 1) * U * VPL * G * 16);
-            const Scalar vw = pick_val(k * U);
+            if (ends == 0) {
+                // the batch is full and inside one row
 #pragma unroll
-            for (int j = 0; j < U; ++j) {
-                if (j < nvalid) {
-                    const Scalar v = __shfl_sync(gmask, vw, (k * U + j) % G, G);
+                for (int j = 0; j < U; ++j)
 #pragma unroll
                     for (int q = 0; q < VPL; ++q)
-                        if (FULL || gl + q * G < NV) F::run(acc[q], v, lds16(slot0 + (j * VPL + q) * G * 16));
-                }
-                if ((ends >> j) & 1u) {
-                    if (head_pending || ((tails >> j) & 1u)) {
-                        float *prow = a.partial + ((u - a.unit_begin) * 2 + (head_pending ? 0 : 1)) * a.N;
+                        if (FULL || gl + q * G < NV)
+                            BatchFma<T>::run(acc[q], vw, j, lds16(slot0 + (j * VPL + q) * G * 16));
+            } else {
 #pragma unroll
-                        for (int q = 0; q < VPL; ++q) {
-                            const int vi = gl + q * G;
-                            if (!FULL && vi >= NV) continue;
-                            float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
+                for (int j = 0; j < U; ++j) {
+                    if (j < nvalid) {
 #pragma unroll
-                            for (int e = 0; e < EPV; e += 4)
-                                dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
-                        }
-                        head_pending = false;
-                    } else {
-                        const int64_t row = __shfl_sync(gmask, myrow, j, G);
-#pragma unroll
-                        for (int q = 0; q < VPL; ++q) {
-                            const int vi = gl + q * G;
-                            if (FULL || vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
-                        }
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV)
+                                BatchFma<T>::run(acc[q], vw, j, lds16(slot0 + (j * VPL + q) * G * 16));
                     }
+                    if ((ends >> j) & 1u) {
+                        if (head_pending || ((tails >> j) & 1u)) {
+                            float *prow = a.partial + ((u - a.unit_begin) * 2 + (head_pending ? 0 : 1)) * a.N;
 #pragma unroll
-                    for (int q = 0; q < VPL; ++q)
+                            for (int q = 0; q < VPL; ++q) {
+                                const int vi = gl + q * G;
+                                if (!FULL && vi >= NV) continue;
+                                float4 *dst = reinterpret_cast<float4 *>(prow + (int64_t)vi * EPV);
 #pragma unroll
-                        for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                                for (int e = 0; e < EPV; e += 4)
+                                    dst[e / 4] = make_float4(acc[q][e], acc[q][e + 1], acc[q][e + 2], acc[q][e + 3]);
+                            }
+                            head_pending = false;
+                        } else {
+                            const int64_t row = s_row[buf * U + j];
+#pragma unroll
+                            for (int q = 0; q < VPL; ++q) {
+                                const int vi = gl + q * G;
+                                if (FULL || vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
+                            }
+                        }
+#pragma unroll
+                        for (int q = 0; q < VPL; ++q)
+#pragma unroll
+                            for (int e = 0; e < EPV; ++e) acc[q][e] = 0.f;
+                    }
                 }
             }
-            // consumption moves to the next chunk: B becomes A and the chunk
-            // after it is loaded, 6 batches before the issue stage needs it
+            // chunk n = o0 / CH is finished after its last batch: its slot
+            // takes chunk n + 2 (held in registers), and chunk n + 3 is loaded
             if (((k + 1) * U) % CH == 0) {
-#pragma unroll
-                for (int i = 0; i < PER; ++i) {
-                    colA[i] = colB[i];
-                    valA[i] = valB[i];
-                }
-                ++ka;
-                load_chunk(s0 + (int64_t)(ka + 1) * CH, colB, valB);
+                const int n = o0 / CH;
+                __syncwarp();
+                stage(n & 1, colR, valR);
+                __syncwarp();
+                load_chunk(s0 + (int64_t)(n + 3) * CH, colR, valR);
             }
             issue(k + 2);
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");
     }
 }
+
 
 // Sums the per-unit partials of every row that crosses a unit boundary, in
 // unit order: tail(u0) + head(u0 + 1) + ... + head(u1).  One warp per unit;
@@ -792,15 +956,17 @@ cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
     if constexpr (G >= 16) {
         const int choice = gather_kernel_choice();
         const bool full = a.N / Vec<T>::kElems == G * VPL;
-        if (choice <= 0 && a.K > 0 && G == 32) {
+        if constexpr (G == 32) {
+        if (choice <= 0 && a.K > 0) {
             // ring (measured faster when a whole warp serves one row; half-warp
             // groups stay on the stream kernel): 2 * U positions x VPL
             // vectors per lane, 8 warps per block
-            const size_t smem = (size_t)kGatherThreads * 2 * U * VPL * 16;
+            const size_t smem = (size_t)(kGatherThreads / 32) * RingShape<T, VPL, U>::kWarpBytes;
             constexpr int RMINB = (VPL == 1) ? 3 : 2;
             if (full)
                 return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, true>, a, 32 / G, smem, stream);
             return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, false>, a, 32 / G, smem, stream);
+        }
         }
         if (choice <= 1 && a.K > 0) {
             if (full)
