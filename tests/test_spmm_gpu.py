@@ -279,6 +279,65 @@ torch.save(outs, sys.argv[2])
 """
 
 
+def row_window_csr(K, seed, idt, unit=256):
+    """Row structure aimed at the ring kernel's row-end window: leading and
+    trailing empty rows, runs of 33-100 empty rows between short rows (more
+    row ends in one 8-position batch than one 32-row window holds), empty
+    runs that start exactly at a unit boundary (owned by the next unit),
+    one-nonzero rows (a row end at every position) and a few long rows."""
+    g = np.random.default_rng(seed)
+    deg = [0] * 40
+    nnz = 0
+    while nnz < 24 * unit:
+        d = int(g.choice([1, 1, 2, 3, 5, 9, 17, 40, 300]))
+        deg.append(d)
+        nnz += d
+        if nnz % unit and unit - nnz % unit <= 12:    # land exactly on a unit boundary
+            while nnz % unit:
+                deg.append(1)
+                nnz += 1
+        if nnz % unit == 0:
+            deg += [0] * 45
+        if g.random() < 0.05:
+            deg += [0] * int(g.integers(33, 101))
+    deg += [0] * 70
+    rows = [np.sort(g.choice(K, size=d, replace=False)) for d in deg]
+    crow = np.zeros(len(rows) + 1, np.int64)
+    crow[1:] = np.cumsum([len(r) for r in rows])
+    return torch.from_numpy(crow).to(idt), torch.from_numpy(np.concatenate(rows)).to(idt)
+
+
+@pytest.mark.parametrize("dtype,N,idt", [(torch.float16, 256, torch.int32), (torch.float16, 1024, torch.int64),
+                                         (torch.float32, 128, torch.int32), (torch.float32, 512, torch.int64)])
+def test_ring_row_window_structure(npu, dtype, N, idt):
+    crow, col = row_window_csr(700, N, idt)
+    g = torch.Generator().manual_seed(N)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
+    B = torch.randn(700, N, generator=g).to(dtype)
+    y = csr_call(npu, crow, col, val, B)
+    assert_close(y, oracle.spmm_csr_f64(crow, col, val, B), dtype, f"{dtype} N={N}")
+    y2 = csr_call(npu, crow, col, val, B, "spmm_csr_aiv_mb_batch")
+    assert torch.equal(y, y2)
+    check_status(npu)
+
+
+def test_ring_malformed_row_pointers_are_reported(npu):
+    """Whole-warp rows (ring kernel): a decreasing row pointer and one past
+    nnz are reported through the device status; nothing faults."""
+    K, N = 64, 256
+    B = torch.randn(K, N).half()
+    for crow in ([0, 5, 3, 8], [0, 2, 4, 6, 9, 8], [0, 3, 30]):
+        crow = torch.tensor(crow, dtype=torch.int32)
+        nnz = 8
+        col = torch.arange(nnz, dtype=torch.int32) % K
+        val = torch.ones(nnz).half()
+        npu.device_status(True)
+        csr_call(npu, crow, col, val, B)
+        torch.cuda.synchronize()
+        code, _ = npu.device_status(True)
+        assert code == 2, crow.tolist()
+
+
 def test_cuda_core_kernels_bitwise_identical(npu, tmp_path):
     """The CUDA-core kernels - ring (cp.async ring, mixed-precision
     fma.rn.f32.f16 / packed f32x2 fma), flat stream and row (convert + fmaf) -
@@ -297,6 +356,9 @@ def test_cuda_core_kernels_bitwise_identical(npu, tmp_path):
         g = torch.Generator().manual_seed(N)
         val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
         B = torch.randn(900, N, generator=g).to(dtype)
+        cases.append((crow, col, val, B))
+        crow, col = row_window_csr(900, N + 1, idt)
+        val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
         cases.append((crow, col, val, B))
     src = tmp_path / "in.pt"
     torch.save(cases, src)
