@@ -58,6 +58,11 @@ struct GatherArgs {
     float *partial;     // (unit_end - unit_begin) * 2 * N floats
     int64_t *unit_rows; // (unit_end - unit_begin) + 1 entries of scratch
     DevStatus *status;
+    // Optional, set by the ring kernel's launcher (pointing at unit_rows):
+    // split_rows[u] = the row that starts in unit u and continues past its
+    // end (its tail partial was written), else -1; the fix-up then needs no
+    // search for it.
+    int64_t *split_rows;
 };
 
 // Points a's scratch arrays into a workspace of plan.workspace_bytes().

@@ -613,6 +613,7 @@ csr_ring_kernel(const GatherArgs a)
                 zero_row(r);
             }
         }
+        if (a.split_rows && gl == 0) a.split_rows[u - a.unit_begin] = -1;
         if (!have_row) continue;
         const int64_t s0 = max(lo, beg);
         bool head_pending = beg < lo;   // the first segment is a head partial
@@ -808,6 +809,7 @@ csr_ring_kernel(const GatherArgs a)
                     if ((ends >> j) & 1u) {
                         if (head_pending || ((tails >> j) & 1u)) {
                             float *prow = a.partial + ((u - a.unit_begin) * 2 + (head_pending ? 0 : 1)) * a.N;
+                            if (!head_pending && a.split_rows && gl == 0) a.split_rows[u - a.unit_begin] = rcur;
 #pragma unroll
                             for (int q = 0; q < VPL; ++q) {
                                 const int vi = gl + q * G;
@@ -864,8 +866,13 @@ csr_fixup_kernel(const GatherArgs a)
     for (int64_t u = a.unit_begin + warp; u < a.unit_end - 1; u += nwarps) {
         const int64_t lo = u * a.unit;
         const int64_t hi = lo + a.unit;
-        const int64_t i = warp_lower_bound(rowptr, a.row_begin, a.M + 1, hi);
-        const int64_t r = i - 1;
+        int64_t r;
+        if (a.split_rows) {
+            r = a.split_rows[u - a.unit_begin];   // written by the ring kernel
+            if (r < 0) continue;
+        } else {
+            r = warp_lower_bound(rowptr, a.row_begin, a.M + 1, hi) - 1;
+        }
         if (r < a.row_begin || r >= a.M) continue;
         const int64_t beg = ld_idx(rowptr + r);
         const int64_t end = ld_idx(rowptr + r + 1);
@@ -945,9 +952,11 @@ cudaError_t launch_ring(Kern kern, const GatherArgs &a, int units_per_warp, size
     const int64_t warps_needed = (units + units_per_warp - 1) / units_per_warp;
     int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
     blocks = std::max<int64_t>(1, std::min(blocks, (warps_needed + 7) / 8));
-    kern<<<(unsigned)blocks, kGatherThreads, smem, stream>>>(a);
+    GatherArgs b = a;
+    b.split_rows = a.unit_rows;   // the ring kernel records the split row of each unit
+    kern<<<(unsigned)blocks, kGatherThreads, smem, stream>>>(b);
     e = cudaGetLastError();
-    return e != cudaSuccess ? e : launch_fixup<T, I>(a, stream);
+    return e != cudaSuccess ? e : launch_fixup<T, I>(b, stream);
 }
 
 template <typename T, typename I, int G, int VPL, int U, int MINB>
