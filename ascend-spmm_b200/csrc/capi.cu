@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/spmm_b200.h"
@@ -93,6 +94,34 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     return SPMM_OK;
 }
 
+// Side stream of each device for the mixed operator: its CSR rows beyond
+// the windows run there concurrently with the window kernel (disjoint output
+// rows; the window kernel uses no workspace), joined back by an event.
+// Created on first use and kept for the process; the mutex keeps the
+// record/wait pairs of concurrent callers from interleaving.
+struct SideStream {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mu;
+SideStream g_side[128];
+
+cudaError_t side_stream(SideStream **out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+    SideStream &x = g_side[dev];
+    if (!x.stream) {
+        if ((e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming)) != cudaSuccess) return e;
+    }
+    *out = &x;
+    return cudaSuccess;
+}
+
 size_t mixed_workspace(int64_t v_nnz, int64_t N, int dtype)
 {
     return spmmb::plan_gather(v_nnz, N, dtype).workspace_bytes();
@@ -123,6 +152,17 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
     spmmb::DevStatus *st = spmmb::device_status_ptr(&e);
     if (!st) return cuda_error(e, op);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool both = n_windows > 0 && v_rows > 16 * n_windows;
+    std::unique_lock<std::mutex> lock(g_side_mu, std::defer_lock);
+    SideStream *side = nullptr;
+    cudaStream_t sg = s;   // stream of the CSR rows
+    if (both) {
+        lock.lock();
+        if ((e = side_stream(&side)) != cudaSuccess) return cuda_error(e, op);
+        if ((e = cudaEventRecord(side->fork, s)) != cudaSuccess) return cuda_error(e, op);
+        if ((e = cudaStreamWaitEvent(side->stream, side->fork, 0)) != cudaSuccess) return cuda_error(e, op);
+        sg = side->stream;
+    }
     if (n_windows > 0) {
         spmmb::WindowArgs w{};
         w.cptr = Crowptr; w.ccol = Ccol; w.cval = Cvalue;
@@ -141,7 +181,12 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
         a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
         spmmb::set_workspace(a, plan, workspace);
         a.status = st;
-        e = spmmb::launch_gather(a, itype, dtype, batch_depth, s);
+        e = spmmb::launch_gather(a, itype, dtype, batch_depth, sg);
+        if (both) {   // join even after a launch error, so s never races the side stream
+            const cudaError_t e1 = cudaEventRecord(side->join, sg);
+            const cudaError_t e2 = e1 == cudaSuccess ? cudaStreamWaitEvent(s, side->join, 0) : e1;
+            if (e == cudaSuccess) e = e2;
+        }
         if (e != cudaSuccess) return cuda_error(e, op);
     }
     return SPMM_OK;
