@@ -555,8 +555,10 @@ cudaError_t launch_ww_f32(const WindowArgs &a, cudaStream_t stream)
     if (e != cudaSuccess) return e;
     const int nslices = (int)(a.N / 128);
     const int64_t items = a.nwin * nslices;
-    int64_t blocks = (int64_t)std::max(per_sm, 1) * device_sm_count();
-    blocks = std::max<int64_t>(1, std::min(blocks, (items + WARPS - 1) / WARPS));
+    // one item per warp, no persistent loop: the block scheduler balances
+    // windows of very different sizes (measured 4.5 % faster on config 4)
+    (void)per_sm;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((items + WARPS - 1) / WARPS, INT_MAX));
     kern<<<(unsigned)blocks, WARPS * 32, L::kBlock, stream>>>(a, nslices);
     return cudaGetLastError();
 }
