@@ -8,7 +8,6 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
-#include <mutex>
 #include <string>
 
 #include "../../include/spmm_b200.h"
@@ -94,17 +93,17 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     return SPMM_OK;
 }
 
-// Side stream of each device for the mixed operator: its CSR rows beyond
-// the windows run there concurrently with the window kernel (disjoint output
-// rows; the window kernel uses no workspace), joined back by an event.
-// Created on first use and kept for the process; the mutex keeps the
-// record/wait pairs of concurrent callers from interleaving.
+// Side stream of each (host thread, device) for the mixed operator: its CSR
+// rows beyond the windows run there concurrently with the window kernel
+// (disjoint output rows; the window kernel uses no workspace), forked from
+// and joined back to the caller's stream by events.  Per host thread, so
+// callers on different threads (and a stream capture on one of them) never
+// share one; created on first use and kept for the thread's lifetime.
 struct SideStream {
     cudaStream_t stream = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
 };
-std::mutex g_side_mu;
-SideStream g_side[128];
+thread_local SideStream g_side[128];
 
 cudaError_t side_stream(SideStream **out)
 {
@@ -153,11 +152,9 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
     if (!st) return cuda_error(e, op);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool both = n_windows > 0 && v_rows > 16 * n_windows;
-    std::unique_lock<std::mutex> lock(g_side_mu, std::defer_lock);
     SideStream *side = nullptr;
     cudaStream_t sg = s;   // stream of the CSR rows
     if (both) {
-        lock.lock();
         if ((e = side_stream(&side)) != cudaSuccess) return cuda_error(e, op);
         if ((e = cudaEventRecord(side->fork, s)) != cudaSuccess) return cuda_error(e, op);
         if ((e = cudaStreamWaitEvent(side->stream, side->fork, 0)) != cudaSuccess) return cuda_error(e, op);

@@ -207,6 +207,62 @@ def test_mixed_random_windows(npu, dtype, N):
     check_status(npu)
 
 
+def test_mixed_op_graph_capture_and_threads(npu):
+    """The mixed operator forks its CSR rows onto an internal side stream: a
+    CUDA graph capture records the fork and replays to the eager bits, and
+    host threads calling it on their own streams get the same bits."""
+    import threading
+
+    crow, col = rand_csr(900, 700, 0.03, seed=5, long_rows={3: 600, 880: 500}, empty_every=9)
+    g = torch.Generator().manual_seed(5)
+    val = (torch.rand(col.numel(), generator=g) * 2 - 1).half()
+    B = torch.randn(700, 128, generator=g).half().to(DEV)
+    m = npu.preprocess(crow.to(DEV), col.to(DEV), val.to(DEV), 900, 700, 16, False)
+    assert m["crow_window_ptr"].numel() > 1 and m["vrow_window_ptr"].numel() - 1 > 16 * (m["crow_window_ptr"].numel() - 1)
+
+    def call():
+        return mixed_call(npu, m, B)
+
+    eager = call()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            call()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = call()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, eager)
+
+    outs = [None] * 4
+    errors = []
+
+    def work(i):
+        try:
+            st = torch.cuda.Stream()
+            with torch.cuda.stream(st):
+                for _ in range(5):
+                    outs[i] = call()
+            st.synchronize()
+        except Exception as exc:   # surfaced below
+            errors.append(exc)
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    for o in outs:
+        assert torch.equal(o, eager)
+    check_status(npu)
+
+
 # ------------------------------------------------------ failure handling
 
 def test_invalid_columns_are_reported_not_faulted(npu):
