@@ -33,8 +33,9 @@ struct GatherPlan {
     int64_t nunits() const { return unit_end - unit_begin; }
     // fp32 head/tail partial rows, two per unit
     size_t partial_bytes() const { return (size_t)nunits() * 2 * (size_t)N * sizeof(float); }
-    // then the first row of every unit boundary (int64, nunits + 1 entries;
-    // used by the tensor-core kernel)
+    // then one int64 per unit boundary (nunits + 1 entries): the first row of
+    // each unit for the tensor-core kernel, or the split row of each unit
+    // that the ring kernel records for the fix-up
     size_t rows_offset() const { return (partial_bytes() + 255) & ~size_t(255); }
     size_t workspace_bytes() const { return rows_offset() + (size_t)(nunits() + 1) * sizeof(int64_t); }
 };
