@@ -42,9 +42,11 @@ def test_abi_version_and_workspace_queries(lib):
     assert lib.spmm_abi_version() == 1
     lib.spmm_csr_workspace_bytes.restype = ctypes.c_size_t
     lib.spmm_csr_workspace_bytes.argtypes = [ctypes.c_int64] * 3 + [ctypes.c_int]
-    # 163840 nonzeros -> 640 units of 256: two fp32 partial rows of N=128 per
-    # unit, then (640 + 1) int64 first rows of the unit boundaries
-    assert lib.spmm_csr_workspace_bytes(16384, 128, 163840, 0) == 640 * 2 * 128 * 4 + 641 * 8
+    # two fp32 partial rows of N=128 per unit, then one int64 per unit
+    # boundary.  163840 nonzeros: units of 64 (small matrices), 2560 units
+    assert lib.spmm_csr_workspace_bytes(16384, 128, 163840, 0) == 2560 * 2 * 128 * 4 + 2561 * 8
+    # 2^22 nonzeros: units of 256, 16384 units
+    assert lib.spmm_csr_workspace_bytes(1 << 18, 128, 1 << 22, 0) == 16384 * 2 * 128 * 4 + 16385 * 8
 
 
 def test_argument_errors_need_no_gpu(lib):
