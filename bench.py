@@ -34,7 +34,7 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
+from datetime import datetime, timedelta
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -55,7 +55,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", type=int, default=2)
@@ -121,7 +121,12 @@ def allreduce_sum(x: float, world) -> float:
 # --------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock/throttle samples (every 50 ms) of one GPU.  Entering
+    starts the sampler and waits (up to 5 s) for its first sample; mark(t0)
+    and mark(t1) bracket the timed region, and summary() keeps the samples
+    from 0.3 s before it (the warm-up steps that run under the sampler right
+    before timing) to its end."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -129,6 +134,7 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.file = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
@@ -136,6 +142,9 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "50"], stdout=self.file, stderr=subprocess.DEVNULL)
+            t_end = time.time() + 5.0
+            while time.time() < t_end and os.path.getsize(self.file.name) == 0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -148,17 +157,34 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
+    def mark(self, start):
+        if start:
+            self.t0 = datetime.now()
+        else:
+            self.t1 = datetime.now()
+
     def summary(self):
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
-        rows = []
+        rows, every = [], []
         with open(self.file.name) as f:
             for line in f:
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
+                if len(parts) < 10:
+                    continue
+                every.append(parts[1:])
+                try:
+                    ts = datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f")
+                except ValueError:
+                    continue
+                if self.t0 is None or self.t1 is None or \
+                        self.t0 - timedelta(seconds=0.3) <= ts <= self.t1 + timedelta(seconds=0.05):
+                    rows.append(parts[1:])
         os.unlink(self.file.name)
+        window = "timed region and the 0.3 s of warm-up before it"
+        if not rows and every:   # timestamps unreadable: keep the whole sampler run
+            rows, window = every, "warm-up and timed region"
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -167,7 +193,8 @@ class ClockSampler:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None,
+                "window": window}
 
 
 def peak_hbm():
@@ -256,22 +283,24 @@ def run_ours(args, rank, world, local):
         return spmm_npu.spmm_ascend_cube(*mixed, B, start[:20], start)
 
     stream = torch.cuda.current_stream()
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    code, detail = spmm_npu.device_status(True)
-    assert code == 0, (code, detail)
+    with ClockSampler(local) as clk:   # sampling from before the warm-up on
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        code, detail = spmm_npu.device_status(True)
+        assert code == 0, (code, detail)
 
-    # ---- device-timed region -------------------------------------------
-    barrier(world)
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+        # ---- device-timed region ---------------------------------------
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clk.mark(True)
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
         torch.cuda.synchronize()
+        clk.mark(False)
     barrier(world)
     ms_local = ev0.elapsed_time(ev1)
     ms_total = allreduce_max(ms_local, world)
