@@ -351,7 +351,7 @@ def run_ours(args, rank, world, local):
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": bytes_local},
         **out,
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": launches_per_step * args.steps if launches_per_step is not None else None,
         "clocks": clk.summary(),
     }
 
@@ -369,12 +369,16 @@ def count_own_kernels(step):
     from torch.profiler import ProfilerActivity, profile
 
     torch.cuda.synchronize()
-    with warnings.catch_warnings():
-        warnings.simplefilter("ignore")
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            step()
-            torch.cuda.synchronize()
-    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    try:
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                step()
+                torch.cuda.synchronize()
+        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    except Exception as exc:   # no CUDA activity tracing in this process
+        print(f"gpu_launches: kernel trace unavailable ({exc})", file=sys.stderr)
+        return None
     return sum(1 for n in names if "spmmb::" in n)
 
 
