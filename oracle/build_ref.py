@@ -19,8 +19,8 @@ CPU build of torch.  No reference source is copied into this repository.
   ``block_level_split`` (custom_op.cpp:1413-1492), which run on CPU tensors.
   Its NPU operators raise if called.
 
-The recipe needs the reference tree (default ``/root/reference``, override with
-``ASCEND_SPMM_REFERENCE``).  When it is absent (e.g. on a GPU box) the build is
+The recipe needs the reference source tree (its location comes from
+``ASCEND_SPMM_REFERENCE``, with the build container's checkout as default).  When it is absent (e.g. on a GPU box) the build is
 skipped and an already-built ``oracle/_ref`` is used as is.
 """
 
