@@ -62,9 +62,11 @@ int check_itype(int itype, const char *op)
     return SPMM_OK;
 }
 
-int csr_impl(const void *rowptr, const void *col, const void *value, const void *dense, void *out,
-             int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
-             size_t workspace_bytes, void *stream, int batch_depth, const char *op)
+}  // namespace
+
+namespace spmmb {
+int check_csr_args(const void *rowptr, const void *col, const void *value, const void *dense, const void *out,
+                   int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype, const char *op)
 {
     int rc = check_dense(dtype, N, dtype == SPMM_F16 ? 16 : 8, op);
     if (rc) return rc;
@@ -73,8 +75,22 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     if (M == 0) return SPMM_OK;
     if (!rowptr || !dense || !out || (nnz > 0 && (!col || !value)))
         return set_error(SPMM_ERR_ARG, "%s: null array", op);
-    if (misaligned(dense) || misaligned(out) || misaligned(workspace))
-        return set_error(SPMM_ERR_ARG, "%s: dense, out and workspace must be 16-byte aligned", op);
+    if (misaligned(dense) || misaligned(out))
+        return set_error(SPMM_ERR_ARG, "%s: dense and out must be 16-byte aligned", op);
+    return SPMM_OK;
+}
+}  // namespace spmmb
+
+namespace {
+
+int csr_impl(const void *rowptr, const void *col, const void *value, const void *dense, void *out,
+             int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
+             size_t workspace_bytes, void *stream, int batch_depth, const char *op)
+{
+    int rc = spmmb::check_csr_args(rowptr, col, value, dense, out, M, K, N, nnz, itype, dtype, op);
+    if (rc || M == 0) return rc;
+    if (misaligned(workspace))
+        return set_error(SPMM_ERR_ARG, "%s: workspace must be 16-byte aligned", op);
     const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype);
     if (workspace_bytes < plan.workspace_bytes() || !workspace)
         return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
@@ -98,24 +114,51 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
 // (disjoint output rows; the window kernel uses no workspace), forked from
 // and joined back to the caller's stream by events.  Per host thread, so
 // callers on different threads (and a stream capture on one of them) never
-// share one; created on first use and kept for the thread's lifetime.
+// share one; created on first use and destroyed when the thread exits (a
+// thread pool that retires threads gives the streams and events back).
 struct SideStream {
     cudaStream_t stream = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
 };
-thread_local SideStream g_side[128];
+constexpr int kMaxSideDevices = 128;
+struct ThreadSideStreams {
+    SideStream dev[kMaxSideDevices];
+    ~ThreadSideStreams()
+    {
+        // Work already queued on a stream completes before its resources are
+        // released; errors (a runtime already unloading at process exit) are
+        // ignored.
+        for (int d = 0; d < kMaxSideDevices; ++d) {
+            SideStream &x = dev[d];
+            if (!x.stream) continue;
+            cudaSetDevice(d);
+            cudaEventDestroy(x.join);
+            cudaEventDestroy(x.fork);
+            cudaStreamDestroy(x.stream);
+            x = SideStream{};
+        }
+    }
+};
+thread_local ThreadSideStreams g_side;
 
 cudaError_t side_stream(SideStream **out)
 {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
-    SideStream &x = g_side[dev];
-    if (!x.stream) {
-        if ((e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking)) != cudaSuccess) return e;
-        if ((e = cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming)) != cudaSuccess) return e;
-        if ((e = cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming)) != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxSideDevices) return cudaErrorInvalidDevice;
+    SideStream &x = g_side.dev[dev];
+    if (!x.stream) {   // all three or none are kept
+        SideStream y;
+        e = cudaStreamCreateWithFlags(&y.stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&y.fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&y.join, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            if (y.fork) cudaEventDestroy(y.fork);
+            if (y.stream) cudaStreamDestroy(y.stream);
+            return e;
+        }
+        x = y;
     }
     *out = &x;
     return cudaSuccess;

@@ -15,6 +15,22 @@ struct DevStatus;
 // Records the thread-local error message of the C ABI and returns `code`.
 int capi_error(int code, const char *fmt, ...);
 
+// Argument contract shared by every CSR entry point (capi.cu): the width and
+// dtype rules of the reference's check_dense_contract (custom_op.cpp:39-57),
+// index type, sizes, null and 16-byte-aligned arrays.  Returns SPMM_OK (also
+// for M == 0, when nothing else is checked) or an error code with the
+// message set.  Workspace checks stay with each entry point.
+int check_csr_args(const void *rowptr, const void *col, const void *value, const void *dense, const void *out,
+                   int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype, const char *op);
+
+// Units of `unit` nonzeros covering nnz (at least one), without the overflow
+// of (nnz + unit - 1) / unit near INT64_MAX.
+inline int64_t units_for(int64_t nnz, int64_t unit)
+{
+    const int64_t n = nnz / unit + (nnz % unit != 0);
+    return n > 0 ? n : 1;
+}
+
 // Per-device sticky status word (status.cu).
 DevStatus *device_status_ptr(cudaError_t *err);
 int device_sm_count();

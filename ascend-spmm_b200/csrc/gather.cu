@@ -1028,12 +1028,12 @@ GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype)
     // nonzeros the floor is 64, so small matrices still spread over all SMs
     // (config 1, 164K nonzeros: 34.9 -> 21.7 us; a floor under 256 measured
     // slower on power-law matrices of 1.6M nonzeros).
-    int64_t target = (nnz + 32767) / 32768;
+    const int64_t target = units_for(nnz, 32768);
     int64_t unit = nnz < (int64_t(1) << 20) ? 64 : 256;
     while (unit < target && unit < 8192) unit <<= 1;
     p.unit = unit;
     p.unit_begin = 0;
-    p.unit_end = std::max<int64_t>(1, (nnz + unit - 1) / unit);
+    p.unit_end = units_for(nnz, unit);
     return p;
 }
 

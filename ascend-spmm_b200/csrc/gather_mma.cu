@@ -10,9 +10,8 @@
 //  * A warp owns (unit, feature slice of FW = 64, 128 or 256 features).  It
 //    walks the unit's positions in chunks of 16.  The 16 gathered B rows of a
 //    chunk (FW features each) are fetched into a per-warp shared-memory ring
-//    by the TMA engine: one cp.async.bulk per row, issued by the lane that
-//    holds the row's column, completing on the stage's mbarrier (rows past
-//    the unit end or with an invalid column are zero-filled instead).  The
+//    by 16-byte cp.async.cg copies (L2 only; rows past the unit end or with
+//    an invalid column are zero-filled), STAGES - 1 chunks ahead.  The
 //    chunk is then one k16 step of
 //        D[feature, row] += sum_k Bg[k, feature] * V[k, row]
 //    with mma.sync m16n8k16 (fp16 x fp16 -> fp32): the A operand is the
@@ -29,8 +28,8 @@
 //    range of window row g, a chunk entry belongs to row g iff it falls in
 //    that range, and the row ends after the window are prefetched into
 //    lanes while the window is multiplied.
-//  * Every mbarrier wait is bounded; on expiry the kernel records
-//    SPMM_DEV_TIMEOUT, drains the copies it issued (again bounded) and stops.
+//  * No wait in the kernel depends on another warp or CTA: cp.async groups
+//    complete on their own.
 //
 // Numerics: per output element the sum runs over the row's nonzeros in
 // 16-position chunks; each chunk's products are exact in fp32 and added by
@@ -56,7 +55,6 @@ namespace spmmb {
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
-constexpr int kSpinLimit = 1 << 22;   // bounded mbarrier polls
 
 __device__ __forceinline__ void ldsm_x4_trans(unsigned addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3)
 {
@@ -89,58 +87,14 @@ __device__ __forceinline__ uint4 lds128(unsigned addr)
     asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
 }
-__device__ __forceinline__ void sts128_zero(unsigned addr)
-{
-    asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(addr), "r"(0) : "memory");
-}
-
-// ---- mbarrier + bulk copy (TMA) ---------------------------------------------
-__device__ __forceinline__ void mbar_init(unsigned addr)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(addr) : "memory");
-}
-__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive_tx(unsigned addr, unsigned bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned addr, unsigned parity)
-{
-    unsigned ok;
-    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
-                 : "=r"(ok)
-                 : "r"(addr), "r"(parity)
-                 : "memory");
-    return ok != 0;
-}
-// Bounded wait for the phase with the given parity: at most kSpinLimit polls
-// and about 2^32 SM cycles (~2 s), whichever ends first; false on expiry.
-__device__ __forceinline__ bool mbar_wait(unsigned addr, unsigned parity)
-{
-    if (mbar_try_wait(addr, parity)) return true;
-    const long long t0 = clock64();
-    for (int i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try_wait(addr, parity)) return true;
-        if (clock64() - t0 > (1ll << 32)) break;
-    }
-    return false;
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-__device__ __forceinline__ void bulk_g2s(unsigned dst, const void *src, unsigned bytes, unsigned mbar)
-{
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(mbar)
-                 : "memory");
-}
-
 template <int FW, int STAGES, int WARPS> struct MmaShape {
     static constexpr int kWarps = WARPS;                      // warps per CTA
     static constexpr int kPitch = FW * 2 + 16;                // bytes per staged row (pad: conflict-free ldmatrix)
     static constexpr int kStage = 16 * kPitch;                // one chunk: 16 gathered rows
     static constexpr int kEpi = 8 * kPitch;                   // 8-row output transpose tile
-    // ring + epilogue tile + one mbarrier per stage, rounded so that every
-    // warp's ring starts 128-byte aligned (bulk copies need 16)
-    static constexpr int kWarp = (STAGES * kStage + kEpi + 8 * STAGES + 127) / 128 * 128;
+    // ring + epilogue tile, rounded so that every warp's ring starts
+    // 128-byte aligned
+    static constexpr int kWarp = (STAGES * kStage + kEpi + 127) / 128 * 128;
     static constexpr int kBlock = kWarps * kWarp;
     static constexpr int kSuper = STAGES / 2 + 3;             // superchunks of columns held in registers
 };
@@ -153,10 +107,9 @@ __device__ __forceinline__ void cp_async16_zfill(unsigned dst, const void *src, 
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// TMA: gathers by cp.async.bulk (one per row) completing on per-stage
-// mbarriers; otherwise by 16-byte cp.async.cg (zero-filling invalid rows)
-// completing per commit group.
-template <typename I, int FW, int STAGES, int WARPS, bool TMA, int MINB>
+// Gathers by 16-byte cp.async.cg (zero-filling invalid rows), completing per
+// commit group.
+template <typename I, int FW, int STAGES, int WARPS, int MINB>
 __global__ void __launch_bounds__(WARPS * 32, MINB)
 csr_mma_kernel(const GatherArgs a, int nslices)
 {
@@ -164,20 +117,11 @@ csr_mma_kernel(const GatherArgs a, int nslices)
     constexpr int PITCH = L::kPitch;
     constexpr int NMT = FW / 16;        // m16 feature tiles per slice
     constexpr int PIECES = FW / 8;      // 16-byte pieces per staged row
-    constexpr unsigned ROWB = FW * 2;   // bytes per gathered row slice
     extern __shared__ __align__(128) unsigned char mma_smem[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const unsigned ring = (unsigned)__cvta_generic_to_shared(mma_smem) + (unsigned)(wid * L::kWarp);
     const unsigned epi = ring + STAGES * L::kStage;
-    const unsigned bars = epi + L::kEpi;
-
-    if constexpr (TMA) {
-        if (lane == 0)
-            for (int s = 0; s < STAGES; ++s) mbar_init(bars + 8 * s);
-        mbar_init_fence();
-        __syncwarp();
-    }
 
     const I *rowptr = static_cast<const I *>(a.rowptr);
     const I *col = static_cast<const I *>(a.col);
@@ -358,32 +302,14 @@ csr_mma_kernel(const GatherArgs a, int nslices)
             return r;
         };
         const char *Bs = B + f0 * 2;
-        // Gathers of chunk c.  TMA: lane 16 (c & 1) + k copies row k.  cp.async:
-        // lane l copies 16-byte pieces l % PIECES, rows l / PIECES + 32 i / PIECES.
+        // Gathers of chunk c: lane l copies 16-byte pieces l % PIECES of rows
+        // l / PIECES + 32 i / PIECES; one commit group per chunk (empty past
+        // the walk, so the group count stays uniform).
         auto issue = [&](int c, int cc) {
-            if (c >= nchunks) {
-                if constexpr (!TMA) cp_commit();
-                return;
-            }
-            const uint32_t gc = gbase + (uint32_t)c;
-            const unsigned st = ring + (gc % STAGES) * L::kStage;
-            const int half = 16 * (c & 1);
-            if constexpr (TMA) {
-                const unsigned mb = bars + 8 * (gc % STAGES);
-                const int k = lane - half;
-                const bool mine = (unsigned)k < 16u;
-                const bool valid = mine && cc >= 0;
-                const unsigned vmask = __ballot_sync(kFull, valid);
-                if (lane == half) mbar_arrive_tx(mb, (unsigned)__popc(vmask) * ROWB);
-                __syncwarp();
-                fence_proxy_async();   // earlier generic reads/writes of this stage precede the bulk writes
-                if (valid) {
-                    bulk_g2s(st + (unsigned)(k * PITCH), Bs + (int64_t)cc * rowbytes, ROWB, mb);
-                } else if (mine) {
-#pragma unroll 4
-                    for (int v = 0; v < PIECES; ++v) sts128_zero(st + (unsigned)(k * PITCH + v * 16));
-                }
-            } else {
+            if (c < nchunks) {
+                const uint32_t gc = gbase + (uint32_t)c;
+                const unsigned st = ring + (gc % STAGES) * L::kStage;
+                const int half = 16 * (c & 1);
                 constexpr int RPI = 32 / PIECES;   // rows per instruction
                 const int v = lane % PIECES;
 #pragma unroll
@@ -393,13 +319,8 @@ csr_mma_kernel(const GatherArgs a, int nslices)
                     const char *src = Bs + (int64_t)(ck >= 0 ? ck : 0) * rowbytes + v * 16;
                     cp_async16_zfill(st + (unsigned)(k * PITCH + v * 16), src, ck >= 0);
                 }
-                cp_commit();
             }
-        };
-        auto wait_chunk = [&](uint32_t gc) -> bool {
-            if constexpr (TMA) return mbar_wait(bars + 8 * (gc % STAGES), (gc / STAGES) & 1u);
-            cp_wait<STAGES - 2>();
-            return true;
+            cp_commit();
         };
 
 #pragma unroll
@@ -409,12 +330,8 @@ csr_mma_kernel(const GatherArgs a, int nslices)
         int c = 0;
         for (; c < nchunks && ok; ++c) {
             const uint32_t gc = gbase + (uint32_t)c;
-            if (!wait_chunk(gc)) {
-                if (lane == 0) raise_status(a.status, SPMM_DEV_TIMEOUT, s0 + 16 * c);
-                ok = false;
-                break;
-            }
-            __syncwarp();
+            cp_wait<STAGES - 2>();   // this lane's copies of chunk c have landed
+            __syncwarp();            // ... and every other lane's
             issue(c + STAGES - 1, col_of(c + STAGES - 1, c));
             const unsigned vc = valq[0];
             const int vh = 16 * (c & 1);
@@ -456,17 +373,10 @@ csr_mma_kernel(const GatherArgs a, int nslices)
             }
         }
         if (ok) flush();
-        // Chunks issued but not consumed (only after a failure): wait them
-        // out (bounded) so no copy lands after the warp moves on.
+        // Chunks issued but not consumed (only after a bad row pointer) land
+        // before the warp moves on.
         const int issued = min(nchunks, c + STAGES - 1);
-        if constexpr (TMA) {
-            for (int x = ok ? nchunks : c; x < issued; ++x) {
-                const uint32_t gx = gbase + (uint32_t)x;
-                mbar_wait(bars + 8 * (gx % STAGES), (gx / STAGES) & 1u);
-            }
-        } else {
-            cp_wait<0>();
-        }
+        cp_wait<0>();
         gbase += (uint32_t)issued;
         __syncwarp();
         if (!ok) break;
@@ -488,12 +398,12 @@ __global__ void __launch_bounds__(256) unit_rows_kernel(const GatherArgs a)
     }
 }
 
-template <typename I, int FW, int STAGES, int WARPS, bool TMA>
+template <typename I, int FW, int STAGES, int WARPS>
 cudaError_t launch_fw(const GatherArgs &a, cudaStream_t stream)
 {
     using L = MmaShape<FW, STAGES, WARPS>;
     constexpr int MINB = std::max(1, (220 * 1024) / L::kBlock);
-    auto kern = csr_mma_kernel<I, FW, STAGES, WARPS, TMA, MINB>;
+    auto kern = csr_mma_kernel<I, FW, STAGES, WARPS, MINB>;
     constexpr int smem = L::kBlock;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -508,14 +418,14 @@ cudaError_t launch_fw(const GatherArgs &a, cudaStream_t stream)
     return cudaGetLastError();
 }
 
-// Variant for measurement: SPMM_B200_MMA = <loader><width>s<stages>, e.g.
-// "c128s6" (cp.async, 128-feature slices, 6 stages) or "t256s4" (TMA bulk).
+// Variant for measurement: SPMM_B200_MMA = c<width>s<stages>, e.g. "c128s6"
+// (128-feature slices, 6 stages, one warp per CTA).
 int mma_variant()
 {
     static const int v = [] {
         const char *e = getenv("SPMM_B200_MMA");
         if (!e) return 0;
-        static const char *names[] = {"", "c128s6", "c128s8", "c64s8", "c256s4", "c256s6", "t128s6", "t256s4", "t256s6", "c128s3"};
+        static const char *names[] = {"", "c128s6", "c128s8", "c64s8", "c256s4", "c256s6", "c128s3"};
         for (int i = 1; i < (int)(sizeof(names) / sizeof(names[0])); ++i)
             if (strcmp(e, names[i]) == 0) return i;
         return 0;
@@ -527,19 +437,16 @@ template <typename I>
 cudaError_t launch_width(const GatherArgs &a, bool deep, cudaStream_t stream)
 {
     switch (mma_variant()) {
-    case 1: if (a.N % 128 == 0) return launch_fw<I, 128, 6, 1, false>(a, stream); break;
-    case 2: if (a.N % 128 == 0) return launch_fw<I, 128, 8, 1, false>(a, stream); break;
-    case 3: return launch_fw<I, 64, 8, 1, false>(a, stream);
-    case 4: if (a.N % 256 == 0) return launch_fw<I, 256, 4, 1, false>(a, stream); break;
-    case 5: if (a.N % 256 == 0) return launch_fw<I, 256, 6, 1, false>(a, stream); break;
-    case 6: if (a.N % 128 == 0) return launch_fw<I, 128, 6, 1, true>(a, stream); break;
-    case 7: if (a.N % 256 == 0) return launch_fw<I, 256, 4, 1, true>(a, stream); break;
-    case 8: if (a.N % 256 == 0) return launch_fw<I, 256, 6, 1, true>(a, stream); break;
-    case 9: if (a.N % 128 == 0) return launch_fw<I, 128, 3, 4, false>(a, stream); break;
+    case 1: if (a.N % 128 == 0) return launch_fw<I, 128, 6, 1>(a, stream); break;
+    case 2: if (a.N % 128 == 0) return launch_fw<I, 128, 8, 1>(a, stream); break;
+    case 3: return launch_fw<I, 64, 8, 1>(a, stream);
+    case 4: if (a.N % 256 == 0) return launch_fw<I, 256, 4, 1>(a, stream); break;
+    case 5: if (a.N % 256 == 0) return launch_fw<I, 256, 6, 1>(a, stream); break;
+    case 6: if (a.N % 128 == 0) return launch_fw<I, 128, 3, 4>(a, stream); break;
     default: break;
     }
-    if (a.N % 128 == 0) return deep ? launch_fw<I, 128, 4, 4, false>(a, stream) : launch_fw<I, 128, 3, 4, false>(a, stream);
-    return deep ? launch_fw<I, 64, 4, 4, false>(a, stream) : launch_fw<I, 64, 3, 4, false>(a, stream);
+    if (a.N % 128 == 0) return deep ? launch_fw<I, 128, 4, 4>(a, stream) : launch_fw<I, 128, 3, 4>(a, stream);
+    return deep ? launch_fw<I, 64, 4, 4>(a, stream) : launch_fw<I, 64, 3, 4>(a, stream);
 }
 
 }  // namespace
@@ -561,7 +468,7 @@ cudaError_t launch_gather_mma(GatherArgs &a, int itype, int batch_depth, cudaStr
     // them).  Like the original split, this depends on nnz only.
     if (a.unit_begin == 0) {
         a.unit *= 2;
-        a.unit_end = std::max<int64_t>(1, (a.nnz + a.unit - 1) / a.unit);
+        a.unit_end = units_for(a.nnz, a.unit);
     }
     {
         const int64_t n = a.unit_end - a.unit_begin + 1;

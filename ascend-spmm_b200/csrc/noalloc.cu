@@ -76,26 +76,14 @@ extern "C" int spmm_csr_launch_noalloc(const void *rowptr, const void *col, cons
 {
     using namespace spmmb;
     const char *op = "spmm_csr_launch_noalloc";
-    // The width/dtype contract of spmm_csr (extension/custom_op.cpp:39-57).
-    if (dtype != SPMM_F16 && dtype != SPMM_F32)
-        return capi_error(SPMM_ERR_ARG, "%s supports only FP16 and FP32 dense tensors", op);
-    const int64_t max_width = dtype == SPMM_F16 ? 1024 : 512, align = dtype == SPMM_F16 ? 16 : 8;
-    if (N <= 0 || N > max_width || N % align)
-        return capi_error(SPMM_ERR_ARG, "%s requires 0 < feature width <= %lld divisible by %lld, but got %lld", op,
-                          (long long)max_width, (long long)align, (long long)N);
-    if (itype != SPMM_I32 && itype != SPMM_I64)
-        return capi_error(SPMM_ERR_ARG, "%s: index arrays must be int32 or int64", op);
-    if (M < 0 || K < 0 || nnz < 0) return capi_error(SPMM_ERR_ARG, "%s: negative size", op);
-    if (M == 0) return SPMM_OK;
-    if (!rowptr || !dense || !out || (nnz > 0 && (!col || !value)))
-        return capi_error(SPMM_ERR_ARG, "%s: null array", op);
-    if (((uintptr_t)dense | (uintptr_t)out) & 15u)
-        return capi_error(SPMM_ERR_ARG, "%s: dense and out must be 16-byte aligned", op);
+    // The same argument contract as spmm_csr_launch (one shared check).
+    const int rc = check_csr_args(rowptr, col, value, dense, out, M, K, N, nnz, itype, dtype, op);
+    if (rc || M == 0) return rc;
 
     GatherPlan plan = plan_gather(nnz, N, dtype);
     while (plan.workspace_bytes() > kNoallocScratchBytes && plan.unit < kNoallocMaxUnit) {
         plan.unit *= 2;
-        plan.unit_end = std::max<int64_t>(1, (nnz + plan.unit - 1) / plan.unit);
+        plan.unit_end = units_for(nnz, plan.unit);
     }
     if (plan.workspace_bytes() > kNoallocScratchBytes)
         return capi_error(SPMM_ERR_UNSUPPORTED,

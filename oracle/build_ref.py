@@ -19,9 +19,12 @@ CPU build of torch.  No reference source is copied into this repository.
   ``block_level_split`` (custom_op.cpp:1413-1492), which run on CPU tensors.
   Its NPU operators raise if called.
 
-The recipe needs the reference source tree (its location comes from
-``ASCEND_SPMM_REFERENCE``, with the build container's checkout as default).  When it is absent (e.g. on a GPU box) the build is
-skipped and an already-built ``oracle/_ref`` is used as is.
+The recipe needs the reference source tree.  Its location comes from the
+environment variable ``ASCEND_SPMM_REFERENCE``, else from the
+``reference_path`` entry of the repository's ``BASELINE.json`` (the record of
+where the reference checkout of this build lives).  When neither names an
+existing tree (e.g. on a GPU box) the build is skipped and an already-built
+``oracle/_ref`` is used as is.
 """
 
 from __future__ import annotations
@@ -37,8 +40,18 @@ OUT_DIR = HERE / "_ref"
 MODULE = "ref_custom_ops_lib"
 
 
-def reference_root() -> Path:
-    return Path(os.environ.get("ASCEND_SPMM_REFERENCE", "/root/reference"))
+def reference_root() -> Path | None:
+    """The reference source tree, or None when no location is recorded."""
+    env = os.environ.get("ASCEND_SPMM_REFERENCE")
+    if env:
+        return Path(env)
+    try:
+        import json
+
+        recorded = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+    except (OSError, ValueError):
+        recorded = None
+    return Path(recorded) if recorded else None
 
 
 def built_path() -> Path:
@@ -53,8 +66,9 @@ def build(force: bool = False, verbose: bool = False) -> Path | None:
     tree nor a previous build is available.
     """
     out = built_path()
-    src = reference_root() / "extension" / "custom_op.cpp"
-    if not src.is_file():
+    root = reference_root()
+    src = root / "extension" / "custom_op.cpp" if root is not None else None
+    if src is None or not src.is_file():
         return out if out.is_file() else None
     if out.is_file() and not force and out.stat().st_mtime >= src.stat().st_mtime:
         return out

@@ -92,20 +92,20 @@ def test_payload_roundtrip_and_checks(tmp_path):
             tm.load_payload(q)
 
     ok = {"shape": (50, 40), "crow_indices": crow.to(torch.int64), "col_indices": col.to(torch.int64)}
-    bad({"shape": (50, 40)}, "missing payload fields: col_indices, crow_indices")
-    bad({**ok, "shape": (0, 40)}, r"invalid matrix shape")
-    bad({**ok, "crow_indices": crow[:-1].to(torch.int64)}, "crow_indices must contain rows \\+ 1 entries")
-    bad({**ok, "col_indices": col[:-1].to(torch.int64)}, "invalid CSR pointer or column array")
+    bad({"shape": (50, 40)}, r"payload lacks field\(s\): col_indices, crow_indices")
+    bad({**ok, "shape": (0, 40)}, "matrix shape must be positive")
+    bad({**ok, "crow_indices": crow[:-1].to(torch.int64)}, "crow_indices needs rows \\+ 1")
+    bad({**ok, "col_indices": col[:-1].to(torch.int64)}, "crow_indices must run from 0")
     c3 = crow.to(torch.int64).clone()
     a10, a11 = int(c3[10]), int(c3[11])
     c3[10], c3[11] = a11 + 1, a10
-    bad({**ok, "crow_indices": c3}, "nondecreasing|invalid CSR")
+    bad({**ok, "crow_indices": c3}, "decreases|must run from 0")
     k3 = col.to(torch.int64).clone()
     k3[0] = 40
-    bad({**ok, "col_indices": k3}, "out-of-range index")
-    bad({**ok, "nnz": col.numel() + 1}, "payload nnz does not match")
+    bad({**ok, "col_indices": k3}, "col_indices must lie in")
+    bad({**ok, "nnz": col.numel() + 1}, "declares nnz")
     bad({"shape": (3, 3), "crow_indices": torch.zeros(4, dtype=torch.int64),
-         "col_indices": torch.zeros(0, dtype=torch.int64)}, "empty matrices are not supported")
+         "col_indices": torch.zeros(0, dtype=torch.int64)}, "no stored entries")
 
 
 def test_convert_matrix_market(tmp_path):
@@ -133,10 +133,19 @@ def test_discover_and_seed(tmp_path):
     assert [p.name for p in tm.discover_datasets(tmp_path, name="a")] == ["a.pt", "other.pt"]
     assert tm.discover_datasets(tmp_path, index=2)[0].name == "b.pt"
     assert len(tm.discover_datasets(tmp_path, start=1, limit=1)) == 1
-    with pytest.raises(ValueError, match="outside the discovered range"):
+    with pytest.raises(ValueError, match="is not among"):
         tm.discover_datasets(tmp_path, index=3)
     with pytest.raises(ValueError, match="no .pt datasets selected"):
         tm.discover_datasets(tmp_path, name="zzz")
     assert tm.stable_seed(2027, "a/a.pt") == tm.stable_seed(2027, "a/a.pt") != tm.stable_seed(2027, "b/b.pt")
+    import hashlib
+
+    salt = int.from_bytes(hashlib.sha256(b"a/a.pt").digest()[:8], "little")
+    assert tm.stable_seed(2027, "a/a.pt") == (2027 + salt) % (2**63 - 1)
+    for kw, msg in (({"start": -1}, "start must be"), ({"start": 2, "stop": 1}, "must not be below"),
+                    ({"limit": 0}, "limit must be positive")):
+        with pytest.raises(ValueError, match=msg):
+            tm.discover_datasets(tmp_path, **kw)
+    assert [p.name for p in tm.discover_datasets(tmp_path, start=1, stop=3)] == ["other.pt", "b.pt"]
     s = tm.make_start(torch.tensor([0, 5, 5, 9, 20]), 4)
     assert s.dtype == torch.int32 and s.tolist() == oracle.make_start(torch.tensor([0, 5, 5, 9, 20]), 4).tolist()
