@@ -2,26 +2,39 @@
 """Benchmark of the SpMM hot path (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 2] [--op csr|mixed]
+                    [--config 5] [--op csr|mixed|preprocess] [--scaling strong|weak]
 
-One step = one SpMM C = A @ B of BASELINE config 2 (1M x 1M power-law graph,
-~16 nonzeros/row, fp16, N = 256) with its inputs resident in HBM.  With N
-GPUs (torchrun, one rank per GPU) A is row-partitioned, B is replicated and C
-stays row-sharded: no collective runs in the timed region.
+Default step: one SpMM C = A @ B of BASELINE config 5, the largest
+configuration that fits one B200 (16.8M x 16.8M power-law matrix, ~469M
+nonzeros after de-duplication, fp16 values, B = 16.8M x 1024 fp16, about
+72 GB with C), inputs resident in HBM, through ``spmm_csr``.  With N GPUs
+(torchrun, one rank per GPU) the matrix is cut into N row ranges balanced by
+nonzeros at 16-row window boundaries (``--scaling strong``, the default:
+total work fixed) or every rank owns one config-sized row block of a global
+matrix (``--scaling weak``); B is replicated and C stays row-sharded, so no
+collective runs in the timed region.  ``--gather`` times the optional full-C
+all-gather separately.
 
-``--scaling weak`` (default): every rank owns one config-sized row block of a
-global A of N blocks (rank r's block is the config generated with seed
-2027 + r; rank 0's block is the 1-GPU workload) times the shared B (seed
-2027), so the work per GPU is fixed as N grows.  ``--scaling strong``: the
-single config matrix is cut into N row ranges balanced by nonzeros at 16-row
-window boundaries (spmm_dist.shard_bounds).
+The JSON line carries, besides the contract keys:
+* ``roofline``: per-nnz-model bytes (the graded algorithmic figure) over the
+  dominant kernel's time, the compulsory bytes (A and C once, each distinct
+  B row once) over the same time, and the DRAM traffic of one launch from a
+  committed ncu capture (``profiles/traffic.json``) over that time;
+* ``kernels``: per-kernel share of a step from a CUDA activity trace of
+  untimed steps (the dominant kernel's time is the step time times its
+  share);
+* ``e2e``: the same SpMM through ``spmm_csr`` with the inputs copied from
+  pinned host memory and C copied back every step;
+* ``cpu_baseline``: the reference's CPU SpMM path on the box's host cores on
+  a leading-row sample: torch.sparse.mm in fp32 on all threads (the
+  reference's ``cpu_reference``, tests/aic_aiv_ablation/common.py:173-177)
+  and SciPy CSR @ dense single-threaded; the faster one is the value;
+* ``preprocess``: the GPU layout builders against the reference's own
+  compiled CPU preprocessing (single-threaded) on config 2.
 
-``--impl reference`` times the reference's own CPU path for SpMM
-(tests/aic_aiv_ablation/common.py:173-177: torch.sparse.mm in fp32, all
-host threads) on a bounded row sample of the same workload, on rank 0 only.
-
-Rank 0 prints one JSON line.  Inputs (B is 537 MB) are larger than the
-126 MB L2, so no flush runs between steps.
+``--impl reference`` times the reference's CPU SpMM path (torch.sparse.mm,
+fp32, all host threads) on the same leading-row sample, on rank 0 only.
+B (34 GB) is far larger than the 126 MB L2, so no flush runs between steps.
 """
 
 from __future__ import annotations
@@ -50,24 +63,27 @@ import workloads  # noqa: E402
 METRIC = "SpMM GFLOP/s (2*nnz*N) and HBM GB/s vs roofline at 1/2/4/8 B200"
 UNIT = "GFLOP/s"
 FALLBACK_HBM_GBS = 6650.0
+CPU_SAMPLE_NNZ = 8_000_000      # nonzeros of the leading-row CPU sample
 
 
-def parse_args():
+def parse_args(argv=None):
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=1000)
-    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--config", type=int, default=2)
+    p.add_argument("--config", type=int, default=5)
     p.add_argument("--scale", type=float, default=1.0)
-    p.add_argument("--op", choices=("csr", "mixed"), default="csr")
-    p.add_argument("--scaling", choices=("weak", "strong"), default="weak")
-    p.add_argument("--e2e-steps", type=int, default=24)
+    p.add_argument("--op", choices=("csr", "mixed", "preprocess"), default="csr")
+    p.add_argument("--scaling", choices=("strong", "weak"), default="strong")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--preprocess-config", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    p.add_argument("--no-preprocess", action="store_true", help="skip the layout-builder leg")
     p.add_argument("--gather", action="store_true",
                    help="also time the optional NCCL all-gather of the row-sharded C (reported separately)")
-    return p.parse_args()
+    return p.parse_args(argv)
 
 
 # --------------------------------------------------------------------------
@@ -96,23 +112,13 @@ def barrier(world):
         dist.barrier()
 
 
-def allreduce_max(x: float, world) -> float:
+def allreduce(x: float, world, op="max") -> float:
     if world == 1:
         return x
     import torch.distributed as dist
 
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
-def allreduce_sum(x: float, world) -> float:
-    if world == 1:
-        return x
-    import torch.distributed as dist
-
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
     return float(t.item())
 
 
@@ -206,68 +212,258 @@ def peak_hbm():
 
 
 def traffic_per_launch(key: str, units: float):
-    """DRAM bytes per launch from a committed ncu summary, scaled by units."""
+    """DRAM bytes of one launch of the dominant kernel, from a committed ncu
+    capture (``profiles/traffic.json``: bytes per nonzero), times units."""
     try:
-        d = json.loads((ROOT / "profiles" / "traffic.json").read_text())
-        e = d[key]
-        return e["dram_bytes_per_unit"] * units
+        e = json.loads((ROOT / "profiles" / "traffic.json").read_text())[key]
+        return e["dram_bytes_per_unit"] * units, e.get("source")
     except Exception:
+        return None, None
+
+
+def value_bytes(dtype) -> int:
+    return torch.finfo(dtype).bits // 8
+
+
+def algorithmic_bytes(M, nnz, N, s) -> int:
+    """Per-nnz gather model: 4(M+1) + nnz(4 + s) + nnz*N*s + M*N*s."""
+    return 4 * (M + 1) + nnz * (4 + s) + nnz * N * s + M * N * s
+
+
+def compulsory_bytes(M, col, N, s, K) -> int:
+    """A once, C once and each distinct B row once."""
+    nnz = int(col.numel())
+    distinct = int((torch.bincount(col.to(torch.int64), minlength=K) > 0).sum()) if nnz else 0
+    return 4 * (M + 1) + nnz * (4 + s) + distinct * N * s + M * N * s
+
+
+# --------------------------------------------------------------------------
+# per-kernel shares from a CUDA activity trace
+# --------------------------------------------------------------------------
+
+def kernel_trace(step, steps=3):
+    """Device time per kernel name of this library (namespace spmmb) over a
+    few untimed steps: {name: (launches per step, microseconds per step)}."""
+    import warnings
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    try:
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                for _ in range(steps):
+                    step()
+                torch.cuda.synchronize()
+        out = {}
+        for e in prof.key_averages():
+            if "spmmb::" not in e.key:
+                continue
+            us = getattr(e, "device_time_total", None)
+            if us is None:
+                us = getattr(e, "cuda_time_total", 0.0)
+            n, t = out.get(e.key, (0, 0.0))
+            out[e.key] = (n + e.count / steps, t + us / steps)
+        return out
+    except Exception as exc:   # no CUDA activity tracing in this process (e.g. under ncu)
+        print(f"kernel trace unavailable ({exc})", file=sys.stderr)
         return None
 
 
+def short_name(kernel: str) -> str:
+    k = kernel.split("(")[0]
+    return k.replace("void ", "").replace("(anonymous namespace)::", "").replace("spmmb::", "")
+
+
 # --------------------------------------------------------------------------
-# CPU baseline: the reference's CPU SpMM (torch.sparse.mm, fp32, all threads)
+# CPU baseline: the reference's CPU SpMM on a leading-row sample
 # --------------------------------------------------------------------------
 
-def cpu_reference_rate(w: "workloads.Workload", target_s=1.0, max_rows=None):
+def cpu_sample(w, target_nnz=CPU_SAMPLE_NNZ):
+    """Rows [0, R) of w holding about target_nnz nonzeros, on the host in
+    fp32, with only the B rows the sample touches (columns relabelled to
+    compact ids; the work - nonzeros and features - is unchanged)."""
+    rp64 = w.rowptr.to(torch.int64)
+    R = int(torch.searchsorted(rp64, torch.tensor([target_nnz], device=rp64.device)).item())
+    R = max(1, min(w.M, R))
+    rp, c, v = workloads.row_slice(w, 0, R)
+    uniq, inv = torch.unique(c.to(torch.int64), return_inverse=True)
+    Bs = w.B.index_select(0, uniq).float().cpu()
+    return {"rows": R, "rowptr": rp.to(torch.int64).cpu(), "col": inv.to(torch.int64).cpu(),
+            "val": v.float().cpu(), "B": Bs, "nnz": int(c.numel()), "distinct_cols": int(uniq.numel()),
+            "desc": f"rows [0, {R}) of {w.name} ({int(c.numel())} of {w.nnz} nonzeros, "
+                    f"{int(uniq.numel())} distinct B rows gathered, N={w.N}); GFLOP/s is "
+                    f"extrapolated to the whole matrix linearly in nonzeros"}
+
+
+FEATURE_CHUNK = 128   # dense columns per CPU library call
+
+
+def feature_chunks(Bs):
+    """B split into contiguous feature blocks: the host libraries address the
+    dense operand with 32-bit offsets (torch.sparse.mm's MKL kernel segfaults
+    past 2^31 elements), so each call gets one block of FEATURE_CHUNK
+    features; the work (2 * nnz * N) is unchanged."""
+    return [Bs[:, f:f + FEATURE_CHUNK].contiguous() for f in range(0, Bs.shape[1], FEATURE_CHUNK)]
+
+
+def torch_cpu_spmm(smp, chunks):
     import oracle
 
+    for Bc in chunks:
+        oracle.cpu_reference(smp["rows"], Bc.shape[0], smp["rowptr"], smp["col"], smp["val"], Bc)
+
+
+def time_runs(fn, budget_s, min_runs=3, max_runs=50):
+    fn()   # warm
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end or len(times) < min_runs) and len(times) < max_runs:
+        t = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t)
+    return statistics.median(times), len(times)
+
+
+def cpu_baseline(w):
+    import scipy.sparse as sp
+
+    smp = cpu_sample(w)
+    chunks = feature_chunks(smp.pop("B"))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    rowptr = w.rowptr.cpu()
-    col, val, B = w.col.cpu(), w.val.cpu(), w.B.cpu()
-    Bf = B.float()
+    flops = 2.0 * smp["nnz"] * w.N
+    t_torch, n_torch = time_runs(lambda: torch_cpu_spmm(smp, chunks), 6.0)
+    A = sp.csr_matrix((smp["val"].numpy(), smp["col"].numpy().astype("int64"), smp["rowptr"].numpy().astype("int64")),
+                      shape=(smp["rows"], chunks[0].shape[0]))
+    Bn = [c.numpy() for c in chunks]
+    t_scipy, n_scipy = time_runs(lambda: [A @ b for b in Bn], 6.0, min_runs=2)
+    legs = {"torch.sparse.mm": {"gflops": round(flops / t_torch / 1e9, 3), "threads": threads, "runs": n_torch},
+            "scipy.csr@dense": {"gflops": round(flops / t_scipy / 1e9, 3), "threads": 1, "runs": n_scipy}}
+    best = max(legs, key=lambda k: legs[k]["gflops"])
+    return {"value": legs[best]["gflops"], "unit": UNIT, "cores": legs[best]["threads"], "kind": "port",
+            "impl": best, "legs": legs, "host_cpus": threads,
+            "sample": smp["desc"] + f"; fp32, dense operand in blocks of {FEATURE_CHUNK} features per call; "
+                                    "median of timed runs",
+            "reference": "tests/aic_aiv_ablation/common.py:173-177 cpu_reference restated (torch.sparse.mm); "
+                         "SciPy single-threaded alongside"}
 
-    def run(rows):
-        rp, c, v = workloads.row_slice(workloads.Workload(w.name, w.M, w.K, w.N, w.dtype, rowptr, col, val, B, {}),
-                                        0, rows)
-        t = time.perf_counter()
-        oracle.cpu_reference(rows, w.K, rp.to(torch.int64), c.to(torch.int64), v, Bf)
-        return time.perf_counter() - t, int(rp[-1])
 
-    rows = min(w.M, max_rows or w.M, 4096)
-    dt, nz = run(rows)
-    while dt < 0.2 and rows < w.M:
-        rows = min(w.M, rows * 4)
-        dt, nz = run(rows)
-    rows = min(w.M, max(1, int(rows * target_s / max(dt, 1e-6))))
-    return rows, threads, Bf, rowptr, col, val
+# --------------------------------------------------------------------------
+# preprocessing: GPU layout builders vs the reference's compiled CPU code
+# --------------------------------------------------------------------------
+
+class native_stdout_silenced:
+    """Sends file descriptor 1 to /dev/null while the reference's compiled
+    builders run (they print block counts from C++), so the bench's JSON
+    line stays the only output."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        self.null = os.open(os.devnull, os.O_WRONLY)
+        os.dup2(self.null, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        os.close(self.null)
+
+
+def preprocess_leg(cfg, dev):
+    """Times each GPU layout builder (CUDA events, median of 5) on config
+    ``cfg`` against the same function of the reference's compiled CPU code
+    (oracle/_ref, single-threaded; the C restatement when it is absent) on
+    the same input, and checks that the layouts agree."""
+    import spmm_npu
+
+    w = workloads.make(cfg, device=dev)
+    M, K = w.M, w.K
+    rp, col, val = w.rowptr, w.col, w.val
+    ratio = (222.0 / 190.0) * 0.5
+    gpu_fns = {
+        "preprocess": lambda: spmm_npu.preprocess(rp, col, val, M, K, 16, False),
+        "preprocess(graph_layout)": lambda: spmm_npu.preprocess(rp, col, val, M, K, 16, True),
+        "csr_to_bcsr": lambda: spmm_npu.csr_to_bcsr(rp, col, val, M, K, 16),
+        "block_level_split": lambda: spmm_npu.block_level_split(rp, col, val, M, K, ratio, 16),
+    }
+    ref, kind = None, "reference"
+    try:
+        import build_ref
+
+        ref = build_ref.load()
+    except Exception as exc:   # the compiled reference could not be loaded here
+        print(f"oracle/_ref unavailable ({exc}); timing the C restatement", file=sys.stderr)
+    if ref is None:
+        import oracle as ref
+        kind = "port"
+    h = [t.cpu() for t in (rp, col, val)]
+    cpu_fns = {
+        "preprocess": lambda: ref.preprocess(*h, M, K, 16, False),
+        "preprocess(graph_layout)": lambda: ref.preprocess(*h, M, K, 16, True),
+        "csr_to_bcsr": lambda: ref.csr_to_bcsr(*h, M, K, 16),
+        "block_level_split": lambda: ref.block_level_split(*h, M, K, ratio, 16),
+    }
+    torch.set_num_threads(1)
+    out = {"config": f"{w.name} M=K={M} nnz={w.nnz} ({w.dtype})", "cpu_kind": kind, "cpu_threads": 1,
+           "builders": {}}
+    for name, fn in gpu_fns.items():
+        got = fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        gms = statistics.median(times)
+        with native_stdout_silenced():
+            t = time.perf_counter()
+            want = cpu_fns[name]()
+            cms = (time.perf_counter() - t) * 1e3
+        same = all(torch.equal(got[k].cpu(), want[k].cpu()) for k in want
+                   if torch.is_tensor(want[k]) and k in got)
+        out["builders"][name] = {"gpu_ms": round(gms, 3), "cpu_ms": round(cms, 1),
+                                 "speedup": round(cms / gms, 1), "layouts_equal": bool(same)}
+    return out
 
 
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
 
-def run_ours(args, rank, world, local):
-    import spmm_npu
-
-    dev = torch.device("cuda", local)
-    from spmm_dist import allgather_rows, shard_bounds
+def local_problem(args, rank, world, dev):
+    """This rank's CSR rows, B and the global nonzero count."""
+    from spmm_dist import shard_bounds
 
     if args.scaling == "weak":
         w = workloads.make(args.config, device=dev, scale=args.scale, seed=workloads.DEFAULT_SEED + rank)
-        B = w.B if rank == 0 else workloads.make(args.config, device=dev, scale=args.scale).B
+        if rank != 0:   # B is the seed-2027 operand on every rank
+            w.B = workloads.make(args.config, device=dev, scale=args.scale).B
         rp, col, val = w.rowptr, w.col, w.val
         bounds = [(k * w.M, (k + 1) * w.M) for k in range(world)]
-        nnz_global = int(allreduce_sum(float(w.nnz), world))
+        nnz_global = int(allreduce(float(w.nnz), world, "sum"))
     else:
         w = workloads.make(args.config, device=dev, scale=args.scale)
         bounds = shard_bounds(w.rowptr, world)
         r0, r1 = bounds[rank]
         rp, col, val = workloads.row_slice(w, r0, r1)
-        B = w.B
         nnz_global = w.nnz
-    rp, col, val = rp.contiguous(), col.contiguous(), val.contiguous()
+    return w, rp.contiguous(), col.contiguous(), val.contiguous(), bounds, nnz_global
+
+
+def run_ours(args, rank, world, local):
+    import spmm_npu
+    from spmm_dist import allgather_rows
+
+    dev = torch.device("cuda", local)
+    w, rp, col, val, bounds, nnz_global = local_problem(args, rank, world, dev)
+    B = w.B
     M_local, nnz_local = int(rp.numel()) - 1, int(col.numel())
     start = torch.zeros(40, dtype=torch.int32, device=dev)
 
@@ -276,6 +472,7 @@ def run_ours(args, rank, world, local):
         m = spmm_npu.preprocess(rp, col, val, M_local, w.K, 16, False)
         mixed = [m[k] for k in ("crow_window_ptr", "unique_col_ids", "value", "vrow_window_ptr",
                                 "vcol_indices", "vvalue")]
+        del m
 
     def step():
         if mixed is None:
@@ -303,19 +500,45 @@ def run_ours(args, rank, world, local):
         clk.mark(False)
     barrier(world)
     ms_local = ev0.elapsed_time(ev1)
-    ms_total = allreduce_max(ms_local, world)
+    ms_total = allreduce(ms_local, world, "max")
     ms_step = ms_total / args.steps
     flops = 2.0 * nnz_global * w.N
     value = flops * args.steps / (ms_total * 1e-3) / 1e9
 
-    # roofline of the dominant kernel (this rank's launches)
-    s = torch.finfo(w.dtype).bits // 8
-    bytes_local = 4 * (M_local + 1) + nnz_local * (4 + s) + nnz_local * w.N * s + M_local * w.N * s
-    achieved = bytes_local / (ms_local / args.steps * 1e-3) / 1e9
+    # ---- per-kernel shares (untimed steps) and the roofline of the dominant kernel
+    trace = kernel_trace(step)
+    kernels = None
+    dom_name, dom_share = None, 1.0
+    if trace:
+        tot = sum(t for _, t in trace.values()) or 1.0
+        kernels = {short_name(k): {"launches_per_step": round(n, 2), "us_per_step": round(t, 1),
+                                   "share": round(t / tot, 4)} for k, (n, t) in trace.items()}
+        dom = max(trace, key=lambda k: trace[k][1])
+        dom_name, dom_share = short_name(dom), trace[dom][1] / tot
+    launches_per_step = sum(n for n, _ in trace.values()) if trace else None
+    s = value_bytes(w.dtype)
+    kernel_s = ms_local / args.steps * 1e-3 * dom_share
+    algo = algorithmic_bytes(M_local, nnz_local, w.N, s)
+    comp = compulsory_bytes(M_local, col, w.N, s, w.K)
     peak, peak_kind = peak_hbm()
-    traffic = traffic_per_launch(f"{w.name}:{args.op}", nnz_local)
+    key = f"{w.name}:{args.op}"
+    traffic, traffic_src = traffic_per_launch(key, nnz_local)
+    roofline = {
+        "bound": "hbm", "achieved": round(algo / kernel_s / 1e9, 1), "peak": peak, "unit": "GB/s",
+        "frac": round(algo / kernel_s / 1e9 / peak, 4),
+        "traffic": round(traffic) if traffic else None,
+        "kernel": dom_name, "kernel_ms": round(kernel_s * 1e3, 4),
+        "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+        "algorithmic_bytes": algo,
+        "algorithmic_model": "per-nnz gather: 4(M+1) + nnz(4+s) + nnz*N*s + M*N*s",
+        "compulsory_bytes": comp,
+        "compulsory_frac": round(comp / kernel_s / 1e9 / peak, 4),
+        "dram_gbs": round(traffic / kernel_s / 1e9, 1) if traffic else None,
+        "dram_frac": round(traffic / kernel_s / 1e9 / peak, 4) if traffic else None,
+        "traffic_source": traffic_src,
+    }
 
-    out = {}
+    extra = {}
     if args.gather and world > 1:
         y = step()
         allgather_rows(y, bounds)
@@ -323,113 +546,110 @@ def run_ours(args, rank, world, local):
         barrier(world)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
-        for _ in range(5):
+        for _ in range(3):
             full = allgather_rows(y, bounds)
         g1.record(stream)
         torch.cuda.synchronize()
-        gms = allreduce_max(g0.elapsed_time(g1), world) / 5
-        out["allgather"] = {"ms": round(gms, 3), "bytes": int(full.numel() * full.element_size()),
-                            "note": "optional full-C all-gather over NCCL, not part of value"}
+        gms = allreduce(g0.elapsed_time(g1), world, "max") / 3
+        extra["allgather"] = {"ms": round(gms, 3), "bytes": int(full.numel() * full.element_size()),
+                              "note": "optional full-C all-gather over NCCL, not part of value"}
+        del y, full
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        extra["cpu_baseline"] = cpu_baseline(w)
     if not args.no_e2e:
-        out["e2e"] = run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops)
+        inputs = [rp, col, val, B] if mixed is None else [*mixed, B]
+        op = ((lambda a: spmm_npu.spmm_csr(*a[:3], a[3], start)) if mixed is None
+              else (lambda a: spmm_npu.spmm_ascend_cube(*a[:6], a[6], start[:20], start)))
+        extra["e2e"] = run_e2e(args, w, inputs, op, dev, world, flops)
+    if rank == 0 and not args.no_preprocess and args.op != "preprocess":
+        extra["preprocess"] = preprocess_leg(args.preprocess_config, dev)
 
-    launches_per_step = count_own_kernels(step)
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f16 (fp32 accumulate)" if s == 2 else "f32",
         "data": "synthetic (seeded generator, BASELINE config shapes)",
-        "config": {"workload": (f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}" if args.scaling == "strong" or world == 1
+        "config": {"workload": (f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}" if args.scaling == "strong"
                                 else f"{world} row blocks of {w.name} (M=K={w.M}, seeds {workloads.DEFAULT_SEED}"
                                      f"+rank), {nnz_global} nnz in all, N={w.N}"),
                    "op": "spmm_csr" if mixed is None else "spmm_ascend_cube(preprocess)",
-                   "parallelism": f"row-shard x{world} (B replicated, C row-sharded)",
+                   "parallelism": f"row-shard x{world} (B replicated, C row-sharded, no collective timed)",
+                   "rank0_rows": M_local, "rank0_nnz": nnz_local,
                    "l2": f"inputs larger than L2 (B {B.numel() * B.element_size() / 1e6:.0f} MB), no flush",
                    "generator": w.params},
-        "gb_per_s": round(bytes_local / (ms_step * 1e-3) / 1e9, 1) if world == 1 else None,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "peak_source": f"{peak_kind} hbm_gbs", "algorithmic_bytes_per_launch": bytes_local},
-        **out,
-        "gpu_launches": launches_per_step * args.steps if launches_per_step is not None else None,
+        "gb_per_s": round(algorithmic_bytes(M_local, nnz_local, w.N, s) / (ms_step * 1e-3) / 1e9, 1),
+        "roofline": roofline,
+        "kernels": kernels,
+        **extra,
+        "gpu_launches": round(launches_per_step * args.steps) if launches_per_step is not None else None,
         "clocks": clk.summary(),
     }
-
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(w)
     if rank == 0:
         print(json.dumps(out), flush=True)
 
 
-def count_own_kernels(step):
-    """Kernels of this library (namespace spmmb) that one step launches,
-    counted from the CUDA activity trace of one untimed step."""
-    import warnings
+def run_e2e(args, w, inputs, op, dev, world, flops):
+    """The same SpMM through the public API with HOST buffers: every step
+    copies the operator's inputs from pinned host memory into device memory,
+    runs the operator and copies C back into pinned host memory, all inside
+    the timed region.
 
-    from torch.profiler import ProfilerActivity, profile
+    One device and one host buffer set (config 5 holds 38 GB of inputs and
+    34 GB of output): the device inputs are the resident tensors,
+    overwritten by identical bytes each step.  Three streams overlap step
+    i's copy of C to the host with step i+1's copy of the inputs; the kernel
+    of step i+1 waits for both (its inputs, and the output buffer being read
+    back), so the steady-state step costs max(H2D, D2H) + kernel."""
+    import psutil
 
+    host_bytes = sum(t.numel() * t.element_size() for t in inputs)
+    out_rows = None
+    y0 = op(inputs)
     torch.cuda.synchronize()
-    try:
-        with warnings.catch_warnings():
-            warnings.simplefilter("ignore")
-            with profile(activities=[ProfilerActivity.CUDA]) as prof:
-                step()
-                torch.cuda.synchronize()
-        names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
-    except Exception as exc:   # no CUDA activity tracing in this process
-        print(f"gpu_launches: kernel trace unavailable ({exc})", file=sys.stderr)
-        return None
-    return sum(1 for n in names if "spmmb::" in n)
+    out_rows, out_bytes = y0.shape[0], y0.numel() * y0.element_size()
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    need = (host_bytes + out_bytes) * local_world
+    avail = psutil.virtual_memory().available
+    # one decision for all ranks (each then takes the same collective steps)
+    fits = allreduce(1.0 if need <= 0.8 * avail else 0.0, world, "min")
+    if fits < 1.0:
+        del y0
+        return {"skipped": f"pinned host buffers of {need / 1e9:.0f} GB for {local_world} local ranks exceed "
+                           f"80% of the {avail / 1e9:.0f} GB of available host memory"}
 
+    def pinned_copy(t):
+        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        return h
 
-def run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops):
-    """Same SpMM through the public API with HOST inputs: every step copies
-    A (rowptr, col, val) and B from pinned host memory, runs spmm_csr and
-    reads C back into pinned host memory, all inside the timed region.
-
-    Steps are pipelined two deep, as a serving loop would run them: step i's
-    host-to-device copies (copy stream) overlap step i-1's kernel and its
-    device-to-host copy of C (a second copy stream), each step with its own
-    buffer set; PCIe carries both directions at once."""
-    import spmm_npu
-
-    M_local = rp.numel() - 1
-    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-    h_in = [pin(t) for t in (rp, col, val, B)]
-    h_out = [torch.empty((M_local, w.N), dtype=w.dtype).pin_memory() for _ in range(2)]
-    d_in = [[torch.empty_like(t, device=dev) for t in (rp, col, val, B)] for _ in range(2)]
+    h_in = [pinned_copy(t) for t in inputs]
+    h_out = torch.empty(y0.shape, dtype=y0.dtype, pin_memory=True)
+    del y0
     s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    comp_done = [torch.cuda.Event() for _ in range(2)]
-    d2h_done = [torch.cuda.Event() for _ in range(2)]
-    started = [False, False]
-    ys = [None, None]
+    in_done, comp_done, d2h_done = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
+    state = {"y": None, "started": False}
 
-    # Buffer reuse is ordered by events (no record_stream): step i's result
-    # replaces that of step i-2 only after its device-to-host copy is done,
-    # so the caching allocator hands the same block back without new
-    # allocations inside the timed region.
-    def e2e_step(i):
-        k = i % 2
+    def e2e_step():
         with torch.cuda.stream(s_in):
-            if started[k]:
-                s_in.wait_event(comp_done[k])          # the kernel of step i-2 has read buffer set k
-            for d, h in zip(d_in[k], h_in):
+            if state["started"]:
+                s_in.wait_event(comp_done)       # the previous kernel has read the inputs
+            for d, h in zip(inputs, h_in):
                 d.copy_(h, non_blocking=True)
-        s_comp.wait_stream(s_in)
+            in_done.record(s_in)
         with torch.cuda.stream(s_comp):
-            if started[k]:
-                s_comp.wait_event(d2h_done[k])         # step i-2's result has been read back
-            ys[k] = None
-            ys[k] = spmm_npu.spmm_csr(*d_in[k][:3], d_in[k][3], start)
-            comp_done[k].record(s_comp)
-        started[k] = True
-        s_out.wait_stream(s_comp)
+            s_comp.wait_event(in_done)
+            if state["started"]:
+                s_comp.wait_event(d2h_done)      # the previous result has been read back
+            state["y"] = None                    # its block may now be handed out again on s_comp
+            state["y"] = op(inputs)
+            comp_done.record(s_comp)
         with torch.cuda.stream(s_out):
-            h_out[k].copy_(ys[k], non_blocking=True)
-            d2h_done[k].record(s_out)
+            s_out.wait_event(comp_done)
+            h_out.copy_(state["y"], non_blocking=True)
+            d2h_done.record(s_out)
+        state["started"] = True
 
-    for i in range(2):
-        e2e_step(i)
+    e2e_step()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
@@ -437,46 +657,36 @@ def run_e2e(args, w, rp, col, val, B, start, step, dev, world, flops):
     e0.record(s_in)
     s_comp.wait_stream(s_in)
     s_out.wait_stream(s_in)
-    for i in range(args.e2e_steps):
-        e2e_step(i)
+    for _ in range(args.e2e_steps):
+        e2e_step()
     s_out.wait_stream(s_in)
     s_out.wait_stream(s_comp)
     e1.record(s_out)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
+    e2e_ms = allreduce(e0.elapsed_time(e1), world, "max")
     e2e_value = flops * args.e2e_steps / (e2e_ms * 1e-3) / 1e9
-    h2d = allreduce_sum(float(sum(t.numel() * t.element_size() for t in h_in)), world)
-    d2h = allreduce_sum(float(h_out[0].numel() * h_out[0].element_size()), world)
-    ref = spmm_npu.spmm_csr(rp, col, val, B, start)
+    h2d = allreduce(float(sum(t.numel() * t.element_size() for t in h_in)), world, "sum")
+    d2h = allreduce(float(out_bytes), world, "sum")
+    # the host copy of the last step equals a resident run (compared in slabs)
+    state["y"] = None
+    ref = op(inputs)
     torch.cuda.synchronize()
-    assert torch.equal(h_out[(args.e2e_steps - 1) % 2].to(dev), ref), "e2e result differs from the resident run"
+    slab = max(1, (1 << 30) // max(1, ref[0].numel() * ref.element_size()))
+    for r in range(0, ref.shape[0], slab):
+        assert torch.equal(h_out[r:r + slab].to(dev), ref[r:r + slab]), "e2e result differs from the resident run"
+    del ref, h_in, h_out
     return {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps,
-            "pipeline": "2 steps in flight: H2D of step i overlaps kernel + D2H of step i-1 (pinned host buffers)"}
+            "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps, "ms_per_step": round(e2e_ms / args.e2e_steps, 2),
+            "pipeline": "pinned host buffers; D2H of step i overlaps H2D of step i+1; device inputs reused"}
 
 
-def cpu_baseline(w):
-    import oracle
-
-    rows, threads, Bf, rowptr, col, val = cpu_reference_rate(w, target_s=1.5)
-    rp, c, v = workloads.row_slice(workloads.Workload(w.name, w.M, w.K, w.N, w.dtype, rowptr, col, val, w.B.cpu(),
-                                                      {}), 0, rows)
-    rp64, c64 = rp.to(torch.int64), c.to(torch.int64)
-    times = []
-    t_end = time.perf_counter() + 12.0
-    while time.perf_counter() < t_end or len(times) < 3:
-        t = time.perf_counter()
-        oracle.cpu_reference(rows, w.K, rp64, c64, v, Bf)
-        times.append(time.perf_counter() - t)
-        if len(times) >= 20:
-            break
-    t = statistics.median(times)
-    gflops = 2.0 * int(rp[-1]) * w.N / t / 1e9
-    return {"value": round(gflops, 3), "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"rows [0, {rows}) of {w.name} ({int(rp[-1])} nnz, N={w.N}), torch.sparse.mm fp32, "
-                      f"median of {len(times)} runs",
-            "impl": "tests/aic_aiv_ablation/common.py:173-177 cpu_reference restated"}
+def run_preprocess_only(args, rank, world, local):
+    if rank != 0:
+        return
+    leg = preprocess_leg(args.preprocess_config, torch.device("cuda", local))
+    print(json.dumps({"metric": "layout builders: GPU vs the reference's CPU preprocessing", "unit": "ms",
+                      "higher_is_better": False, "n_gpus": 1, "preprocess": leg}), flush=True)
 
 
 # --------------------------------------------------------------------------
@@ -486,32 +696,36 @@ def cpu_baseline(w):
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    import oracle
-
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     w = workloads.make(args.config, device=dev, scale=args.scale)
-    rows, threads, Bf, rowptr, col, val = cpu_reference_rate(w, target_s=0.5)
-    rp, c, v = workloads.row_slice(workloads.Workload(w.name, w.M, w.K, w.N, w.dtype, rowptr, col, val, w.B.cpu(),
-                                                      {}), 0, rows)
-    rp64, c64 = rp.to(torch.int64), c.to(torch.int64)
+    smp = cpu_sample(w)
+    workload = f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}"
+    N = w.N
+    del w
+    chunks = feature_chunks(smp.pop("B"))
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+
+    def one():
+        torch_cpu_spmm(smp, chunks)
+
     for _ in range(args.warmup):
-        oracle.cpu_reference(rows, w.K, rp64, c64, v, Bf)
+        one()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.cpu_reference(rows, w.K, rp64, c64, v, Bf)
+        one()
     dt = time.perf_counter() - t0
-    nz = int(rp[-1])
-    value = 2.0 * nz * w.N * args.steps / dt / 1e9
-    sample = f"rows [0, {rows}) of {w.name} ({nz} of {w.nnz} nnz, N={w.N}) per step"
+    value = 2.0 * smp["nnz"] * N * args.steps / dt / 1e9
     out = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded generator, BASELINE config shapes)",
-        "config": {"workload": f"{w.name} M=K={w.M} nnz={w.nnz} N={w.N}", "op": "torch.sparse.mm (cpu_reference)",
+        "config": {"workload": workload, "sample": smp["desc"],
+                   "op": "torch.sparse.mm (the reference's cpu_reference, tests/aic_aiv_ablation/common.py:173-177)",
                    "parallelism": f"host CPU, {threads} threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": smp["desc"] + f" per step; dense operand in blocks of {FEATURE_CHUNK} features"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -523,6 +737,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.op == "preprocess":
+            run_preprocess_only(args, rank, world, local)
         else:
             run_ours(args, rank, world, local)
     finally:

@@ -66,3 +66,35 @@ def test_no_samples_is_reported():
     t0 = datetime(2026, 1, 1, 12, 0, 0)
     s = sampler_with([], t0, t0).summary()
     assert s["sm_mhz"] is None and s["reasons"] == ["no samples"]
+
+
+def test_cpu_sample_keeps_the_product():
+    """The CPU baseline's leading-row sample relabels columns to the B rows it
+    touches; its product equals those rows of A @ B."""
+    import torch
+
+    import oracle
+    import workloads
+
+    bench = load_bench()
+    w = workloads.make(2, scale=0.004)
+    smp = bench.cpu_sample(w, target_nnz=5000)
+    R = smp["rows"]
+    assert smp["nnz"] == int(w.rowptr[R]) and smp["distinct_cols"] == smp["B"].shape[0] <= smp["nnz"]
+    got = oracle.cpu_reference(R, smp["B"].shape[0], smp["rowptr"], smp["col"], smp["val"], smp["B"])
+    rp, c, v = workloads.row_slice(w, 0, R)
+    want = torch.from_numpy(oracle.spmm_csr_f64(rp, c, v, w.B))
+    assert torch.allclose(got.double(), want, atol=1e-4, rtol=1e-4)
+    # the blocked form the bench times computes the same product
+    chunks = bench.feature_chunks(smp["B"])
+    assert sum(b.shape[1] for b in chunks) == w.N and all(b.is_contiguous() for b in chunks)
+    blocked = torch.cat([oracle.cpu_reference(R, b.shape[0], smp["rowptr"], smp["col"], smp["val"], b)
+                         for b in chunks], 1)
+    assert torch.allclose(blocked.double(), want, atol=1e-4, rtol=1e-4)
+
+
+def test_bench_defaults_are_the_headline():
+    bench = load_bench()
+    a = bench.parse_args([])
+    assert (a.config, a.scaling, a.op, a.gpus) == (5, "strong", "csr", 1)
+    assert a.warmup >= 3

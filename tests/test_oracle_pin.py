@@ -74,3 +74,30 @@ def test_oracle_matches_reference(seed):
     same(oracle.block_level_split(ct, cc, vals, nrows, ncols, 0.584, 16), exp["bls"])
     same(oracle.preprocess(ct, cc, vals, nrows, ncols, 16, False), exp["pre"])
     same(oracle.preprocess(ct, cc, vals, nrows, ncols, 16, True), exp["preg"])
+
+
+@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05)])
+def test_oracle_matches_reference_at_config_scale(cfg, scale):
+    """The restatement against the compiled reference on BASELINE-shaped
+    matrices: config 1 at full size (16384 rows, 163840 nonzeros: 1024
+    windows, the marginal-window bucket sort and density sorts over all of
+    them) and config 2 at scale 0.05 (power-law, 52428 rows)."""
+    import workloads
+
+    r = ref()
+    w = workloads.make(cfg, scale=scale)
+    ct, cc, vals = w.rowptr, w.col, w.val
+    with contextlib.redirect_stdout(io.StringIO()):
+        exp = {
+            "bcsr": r.csr_to_bcsr(ct, cc, vals, w.M, w.K, 16),
+            "cube": r.csr_to_ascend_cube(ct, cc, vals, w.M, w.K, 16),
+            "bls": r.block_level_split(ct, cc, vals, w.M, w.K, (222.0 / 190.0) * 0.5, 16),
+            "pre": r.preprocess(ct, cc, vals, w.M, w.K, 16, False),
+            "preg": r.preprocess(ct, cc, vals, w.M, w.K, 16, True),
+        }
+    assert exp["pre"]["unique_col_ids"].numel() > 0 and exp["pre"]["vcol_indices"].numel() > 0
+    same(oracle.csr_to_bcsr(ct, cc, vals, w.M, w.K, 16), exp["bcsr"])
+    same(oracle.csr_to_ascend_cube(ct, cc, vals, w.M, w.K, 16), exp["cube"])
+    same(oracle.block_level_split(ct, cc, vals, w.M, w.K, (222.0 / 190.0) * 0.5, 16), exp["bls"])
+    same(oracle.preprocess(ct, cc, vals, w.M, w.K, 16, False), exp["pre"])
+    same(oracle.preprocess(ct, cc, vals, w.M, w.K, 16, True), exp["preg"])

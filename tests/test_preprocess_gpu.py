@@ -211,3 +211,30 @@ def test_gpu_layouts_drive_spmm(npu):
     assert_close(y[: w.M], ref, torch.float16, "csr_to_bcsr")
     code, detail = npu.device_status(True)
     assert code == 0, (code, detail)
+
+
+@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05)])
+def test_layouts_match_compiled_reference(npu, cfg, scale):
+    """GPU layouts against the reference's own compiled CPU preprocessing
+    (oracle/_ref, built from the reference tree) on config 1 at full size
+    and config 2 at scale 0.05, graph layout included."""
+    import contextlib
+    import io
+
+    import build_ref
+
+    ref = build_ref.load()
+    if ref is None:
+        pytest.skip("the compiled reference preprocessing (oracle/_ref) is not on this machine")
+    w = workloads.make(cfg, scale=scale)
+    got = gpu_funcs(npu, w.M, w.K, w.rowptr, w.col, w.val)
+    with contextlib.redirect_stdout(io.StringIO()):
+        exp = {
+            "csr_to_bcsr": ref.csr_to_bcsr(w.rowptr, w.col, w.val, w.M, w.K, 16),
+            "csr_to_ascend_cube": ref.csr_to_ascend_cube(w.rowptr, w.col, w.val, w.M, w.K, 16),
+            "block_level_split": ref.block_level_split(w.rowptr, w.col, w.val, w.M, w.K, BLOCK_RATIO, 16),
+            "preprocess": ref.preprocess(w.rowptr, w.col, w.val, w.M, w.K, 16, False),
+            "preprocess_graph": ref.preprocess(w.rowptr, w.col, w.val, w.M, w.K, 16, True),
+        }
+    for fn in exp:
+        same_dict(got[fn], exp[fn], f"cfg{cfg}:{fn} vs compiled reference")

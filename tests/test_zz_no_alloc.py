@@ -3,10 +3,15 @@ device memory at call time (an FFI host with a fixed memory budget, or a loop
 that must not let cudaMalloc synchronise the device).  It keeps its scratch
 in a 32 MiB static device array instead of a caller workspace.
 
-Called here through the C ABI (ctypes), on two calls in a row, and checked
-against the workspace entry point spmm_csr_launch with the reference's
-tolerances.  This file is collected last so that a run stopping at the first
-failure has already run every other test; it also passes on its own.
+Called here through the C ABI (ctypes), on calls in a row, and checked
+against the workspace entry point spmm_csr_launch and the float64 oracle with
+the reference's tolerances.  The cases cover every kernel family the entry
+point can reach: the CUDA-core ring kernel (fp16, 1024 features), the
+tensor-core gather (fp16, 128 features) and the stream kernel (fp32, 64
+features, int64 indices); the first two need more partial storage than the
+static array under the default split, so their units are coarsened.  This
+file is collected last so that a run stopping at the first failure has
+already run every other test; it also passes on its own.
 """
 
 import ctypes
@@ -14,6 +19,7 @@ import ctypes
 import pytest
 import torch
 
+import oracle
 from helpers import assert_close, rand_csr
 
 pytestmark = pytest.mark.gpu
@@ -37,16 +43,48 @@ def lib():
     return L
 
 
-def case(seed, M, K, N, dtype, long_rows):
+STATIC_SCRATCH = 32 << 20   # bytes of the library's static scratch array
+
+
+def case(seed, M, K, N, dtype, long_rows, idt=torch.int32):
     g = torch.Generator().manual_seed(seed)
-    crow, col = rand_csr(M, K, 0.01, seed=seed, long_rows=long_rows, empty_every=9)
+    crow, col = rand_csr(M, K, 0.01, seed=seed, long_rows=long_rows, empty_every=9, idt=idt)
     val = (torch.rand(col.numel(), generator=g) * 2 - 1).to(dtype)
     B = torch.randn(K, N, generator=g).to(dtype)
     return crow.cuda(), col.cuda(), val.cuda(), B.cuda()
 
 
+def exact_nnz_case(seed, M, K, N, nnz):
+    """fp16 CSR with exactly nnz nonzeros (distinct sorted columns per row,
+    a few empty rows), built on the device."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    deg = torch.full((M,), nnz // M, dtype=torch.int64, device="cuda")
+    deg[: nnz % M] += 1
+    deg[::101] = 0
+    live = torch.nonzero(deg).flatten()
+    deg[live[: nnz - int(deg.sum())]] += 1   # hand the empty rows' share to the first nonempty ones
+    assert int(deg.sum()) == nnz and int(deg.max()) <= K
+    rows = torch.repeat_interleave(torch.arange(M, device="cuda"), deg)
+    start = torch.cumsum(deg, 0) - deg
+    # row r takes the deg[r] columns (off + k * stride) % K, distinct because stride is odd and K a power of two
+    k = torch.arange(rows.numel(), device="cuda") - start[rows]
+    off = torch.randint(0, K, (M,), generator=g, device="cuda")
+    cols = (off[rows] + k * 2 * (rows % 7) + k) % K
+    key = rows * K + cols
+    key, _ = torch.sort(key)
+    crow = torch.zeros(M + 1, dtype=torch.int64, device="cuda")
+    crow[1:] = torch.cumsum(deg, 0)
+    val = (torch.rand(nnz, generator=g, device="cuda") * 2 - 1).half()
+    B = torch.randn(K, N, generator=g, device="cuda").half()
+    return crow.int(), (key % K).int(), val, B
+
+
 def dtype_code(dtype):
     return 0 if dtype == torch.float16 else 1
+
+
+def itype_code(idt):
+    return 0 if idt == torch.int32 else 1
 
 
 def with_workspace(L, crow, col, val, B):
@@ -55,8 +93,8 @@ def with_workspace(L, crow, col, val, B):
     wbytes = L.spmm_csr_workspace_bytes(M, N, nnz, dtype_code(B.dtype))
     ws = torch.empty(max(wbytes, 1), dtype=torch.uint8, device="cuda")
     rc = L.spmm_csr_launch(crow.data_ptr(), col.data_ptr(), val.data_ptr(), B.data_ptr(), None, 0,
-                           out.data_ptr(), M, K, N, nnz, 0, dtype_code(B.dtype), ws.data_ptr(), wbytes,
-                           torch.cuda.current_stream().cuda_stream)
+                           out.data_ptr(), M, K, N, nnz, itype_code(crow.dtype), dtype_code(B.dtype),
+                           ws.data_ptr(), wbytes, torch.cuda.current_stream().cuda_stream)
     assert rc == 0, L.spmm_last_error()
     return out
 
@@ -65,26 +103,39 @@ def no_alloc(L, crow, col, val, B):
     M, K, N, nnz = crow.numel() - 1, B.shape[0], B.shape[1], col.numel()
     out = torch.empty(M, N, dtype=B.dtype, device="cuda")
     rc = L.spmm_csr_launch_noalloc(crow.data_ptr(), col.data_ptr(), val.data_ptr(), B.data_ptr(),
-                                   out.data_ptr(), M, K, N, nnz, 0, dtype_code(B.dtype),
+                                   out.data_ptr(), M, K, N, nnz, itype_code(crow.dtype), dtype_code(B.dtype),
                                    torch.cuda.current_stream().cuda_stream)
     assert rc == 0, L.spmm_last_error()
     return out
 
 
-def test_no_alloc_matches_workspace_entry_point_two_calls(lib):
-    # call 1: wide rows whose default split needs more partial storage than
-    # the static array, so the unit size is doubled; call 2: a different,
-    # smaller fp32 problem reusing the same array right after.
+def needs_coarser_units(L, c):
+    crow, col, _, B = c
+    return L.spmm_csr_workspace_bytes(crow.numel() - 1, B.shape[1], col.numel(), dtype_code(B.dtype)) > STATIC_SCRATCH
+
+
+def test_no_alloc_matches_workspace_entry_point_and_oracle(lib):
+    # call 1: ring kernel (fp16, 1024 features) whose default split needs
+    # more partial storage than the static array; call 2: tensor-core gather
+    # (fp16, 128 features) at ~2^23 nonzeros, likewise coarsened (and
+    # coarsened again by that kernel); call 3: a small fp32 problem with int64
+    # indices (stream kernel) reusing the same array right after.
     cases = [case(1, 8000, 20000, 1024, torch.float16, {3: 9000, 400: 12000}),
-             case(2, 900, 700, 64, torch.float32, {10: 650, 899: 500})]
+             exact_nnz_case(2, 100_000, 1 << 16, 128, 8_380_000),
+             case(3, 900, 700, 64, torch.float32, {10: 650, 899: 500}, idt=torch.int64)]
+    assert needs_coarser_units(lib, cases[0]) and needs_coarser_units(lib, cases[1])
+    assert not needs_coarser_units(lib, cases[2])
     outs = [no_alloc(lib, *c) for c in cases]
     torch.cuda.synchronize()
-    for c, y in zip(cases, outs):
-        ref = with_workspace(lib, *c)
-        assert_close(y, ref.double().cpu().numpy(), c[3].dtype, "no-alloc vs workspace")
-    # and once more on the first problem after the array held the second one
-    y = no_alloc(lib, *cases[0])
-    assert_close(y, with_workspace(lib, *cases[0]).double().cpu().numpy(), torch.float16, "third call")
+    for i, (c, y) in enumerate(zip(cases, outs)):
+        crow, col, val, B = c
+        assert_close(y, with_workspace(lib, *c).double().cpu().numpy(), B.dtype, f"case {i}: vs workspace")
+        assert_close(y, oracle.spmm_csr_f64(crow.cpu(), col.cpu(), val.cpu(), B.cpu()), B.dtype,
+                     f"case {i}: vs float64 oracle")
+    # and once more on the first two problems after the array held the others
+    for i in (0, 1):
+        y = no_alloc(lib, *cases[i])
+        assert_close(y, with_workspace(lib, *cases[i]).double().cpu().numpy(), torch.float16, f"repeat {i}")
 
 
 def test_no_alloc_rejects_oversized_requests(lib):
