@@ -131,6 +131,11 @@ cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelin
 bool window_warp_eligible(const WindowArgs &a, int dtype);
 cudaError_t launch_window_warp(const WindowArgs &a, int itype, int dtype, cudaStream_t stream);
 
+// Window kernel on tcgen05 tensor cores with TMEM accumulators
+// (window_tc.cu): fp16, N % 128 == 0, 16-byte aligned values, B and out.
+bool window_tc_eligible(const WindowArgs &a, int dtype);
+cudaError_t launch_window_tc(const WindowArgs &a, int itype, cudaStream_t stream);
+
 // ---- spmm_cube (cube.cu) -----------------------------------------------------
 
 struct CubeArgs {

@@ -22,6 +22,7 @@
 // STAGES = 1 is the unpipelined variant (the reference's SPTILE = 16
 // ablation, op_kernel/spmm_ascend_cube_aic_without_pipeline.cpp:6).
 #include <algorithm>
+#include <cstring>
 #include <cstdlib>
 
 #include "../../include/spmm_b200.h"
@@ -389,10 +390,27 @@ cudaError_t launch_f32(const WindowArgs &a, cudaStream_t stream)
 
 }  // namespace
 
+// Window kernel choice: SPMM_B200_WINDOW = block (block-synchronous
+// window.cu kernels), warp (window_warp.cu) or tc (tcgen05, window_tc.cu);
+// the default is the warp-pipelined kernel where eligible.
+int window_kernel_choice()
+{
+    static const int choice = [] {
+        const char *v = getenv("SPMM_B200_WINDOW");
+        if (v && strcmp(v, "block") == 0) return 1;
+        if (v && strcmp(v, "tc") == 0) return 2;
+        if (getenv("SPMM_B200_WINDOW_BLOCK")) return 1;
+        return 0;
+    }();
+    return choice;
+}
+
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined, cudaStream_t stream)
 {
     if (a.nwin <= 0) return cudaSuccess;
-    if (pipelined && window_warp_eligible(a, dtype) && !getenv("SPMM_B200_WINDOW_BLOCK"))
+    if (pipelined && window_kernel_choice() == 2 && window_tc_eligible(a, dtype))
+        return launch_window_tc(a, itype, stream);
+    if (pipelined && window_kernel_choice() != 1 && window_warp_eligible(a, dtype))
         return launch_window_warp(a, itype, dtype, stream);
     if (dtype == SPMM_F16) {
         if (itype == SPMM_I32) return pipelined ? launch_f16<int, 3>(a, stream) : launch_f16<int, 1>(a, stream);

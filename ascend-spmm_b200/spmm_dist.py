@@ -8,13 +8,137 @@ with the single-GPU operators - there is no communication in the SpMM
 itself.  C stays row-sharded; ``allgather_rows`` assembles the full C over
 NCCL (one all-gather for equal shards, one broadcast per rank otherwise) only
 when a caller asks for it.
+
+Failure handling (no GPU fault is involved in any of it): ``Membership``
+keeps the ranks' presence in the process group's store, so a rank that
+leaves between steps is seen by the others on the host before their next
+launch (``RankDeparted``); ``wait_bounded`` gives a collective a deadline
+and aborts the process group when it passes (``CollectiveTimeout``);
+``nccl_options`` makes the NCCL communicator non-blocking, so such an abort
+never waits behind a blocked NCCL call.
 """
 
 from __future__ import annotations
 
+import time
+
 import torch
 
 WINDOW = 16
+
+
+# --------------------------------------------------------------------------
+# failure handling: departed ranks and bounded collectives
+# --------------------------------------------------------------------------
+
+class RankDeparted(RuntimeError):
+    """Another rank left the job between steps (or stopped answering)."""
+
+    def __init__(self, ranks, step):
+        self.ranks = sorted(ranks)
+        self.step = step
+        super().__init__(f"rank(s) {self.ranks} left before step {step}; no collective was entered")
+
+
+class CollectiveTimeout(RuntimeError):
+    """A collective did not complete within its deadline; the process group
+    was aborted."""
+
+
+def nccl_options(nonblocking: bool = True):
+    """Process-group options for the row-sharded job over NCCL.  With
+    ``nonblocking`` the communicator is created non-blocking (ncclConfig_t
+    blocking = 0): NCCL calls return at once, their progress and errors are
+    read through ncclCommGetAsyncError by the process group, and a
+    communicator whose peer is gone can be aborted from the host instead of
+    blocking the calling thread."""
+    import torch.distributed as dist
+
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.config.blocking = 0 if nonblocking else 1
+    return opts
+
+
+def abort_group(group=None) -> bool:
+    """Aborts a process group (NCCL: ncclCommAbort on its communicators,
+    which also ends their device work).  Returns False when the backend
+    offers no abort (then the group's own timeout ends its operations)."""
+    import torch.distributed as dist
+
+    try:
+        dist.distributed_c10d._abort_process_group(group if group is not None else dist.group.WORLD)
+        return True
+    except Exception:   # backend without abort support (e.g. gloo builds)
+        return False
+
+
+def wait_bounded(works, timeout_s: float, group=None, what: str = "collective"):
+    """Waits for async collective handles with a deadline, polling
+    ``is_completed`` (for NCCL a query of the collective's CUDA event, so
+    the host thread never blocks inside NCCL).  On expiry the group is
+    aborted and CollectiveTimeout raised."""
+    works = [w for w in (works if isinstance(works, (list, tuple)) else [works]) if w is not None]
+    deadline = time.monotonic() + timeout_s
+    for w in works:
+        while not w.is_completed():
+            if time.monotonic() > deadline:
+                aborted = abort_group(group)
+                raise CollectiveTimeout(f"{what} did not complete within {timeout_s:.1f} s"
+                                        f"{'; process group aborted' if aborted else ''}")
+            time.sleep(0.0005)
+        w.wait()
+
+
+class Membership:
+    """Which ranks of a row-sharded job are still in it, kept in the process
+    group's key-value store (the TCPStore of torch.distributed), so that no
+    rank enters a collective that a departed peer can never join.
+
+    Each step every rank calls ``enter(step)`` before its first launch: it
+    publishes ``ready/<step>/<rank>`` and waits (bounded, on the host) until
+    every other rank has published the same key or ``left/<rank>``.  A rank
+    that leaves between steps calls ``leave()``; the others then raise
+    RankDeparted at their next ``enter`` instead of hanging in a
+    collective.  A rank that neither arrives nor leaves within ``timeout_s``
+    is reported as departed too."""
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "spmm_dist/", timeout_s: float = 30.0):
+        self.store, self.rank, self.world = store, rank, world
+        self.prefix, self.timeout_s = prefix, timeout_s
+
+    @classmethod
+    def for_default_group(cls, timeout_s: float = 30.0, prefix: str = "spmm_dist/"):
+        import torch.distributed as dist
+
+        return cls(dist.distributed_c10d._get_default_store(), dist.get_rank(), dist.get_world_size(), prefix,
+                   timeout_s)
+
+    def _key(self, *parts) -> str:
+        return self.prefix + "/".join(str(p) for p in parts)
+
+    def _has(self, key: str) -> bool:
+        return bool(self.store.check([key]))
+
+    def leave(self, reason: str = "left") -> None:
+        self.store.set(self._key("left", self.rank), reason)
+
+    def departed(self) -> list:
+        return [r for r in range(self.world) if r != self.rank and self._has(self._key("left", r))]
+
+    def enter(self, step: int) -> None:
+        self.store.set(self._key("ready", step, self.rank), "1")
+        pending = {r for r in range(self.world) if r != self.rank}
+        deadline = time.monotonic() + self.timeout_s
+        while pending:
+            gone = {r for r in pending if self._has(self._key("left", r))}
+            if gone:
+                raise RankDeparted(gone, step)
+            pending = {r for r in pending if not self._has(self._key("ready", step, r))}
+            if not pending:
+                return
+            if time.monotonic() > deadline:
+                raise RankDeparted(pending, step)
+            time.sleep(0.001)
 
 
 def shard_bounds(rowptr: torch.Tensor, world: int) -> list[tuple[int, int]]:
@@ -27,7 +151,7 @@ def shard_bounds(rowptr: torch.Tensor, world: int) -> list[tuple[int, int]]:
     if world <= 1 or M == 0:
         return [(0, M)] + [(M, M)] * max(0, world - 1)
     rp = rowptr.detach().to(torch.int64).cpu()
-    win = rp[::WINDOW]
+    win = rp[::WINDOW].contiguous()
     if int(win[-1]) != int(rp[-1]):
         win = torch.cat([win, rp[-1:]])
     nnz = int(rp[-1])
@@ -46,40 +170,52 @@ def shard_csr(rowptr, col, val, r0: int, r1: int):
     return rp.to(rowptr.dtype).contiguous(), col[p0:p1].contiguous(), val[p0:p1].contiguous()
 
 
-def allgather_rows(local: torch.Tensor, bounds: list[tuple[int, int]], group=None, out=None) -> torch.Tensor:
+def allgather_rows(local: torch.Tensor, bounds: list[tuple[int, int]], group=None, out=None,
+                   timeout_s: float | None = None) -> torch.Tensor:
     """Full C on every rank from row shards ``local`` ([r1 - r0, N] per rank).
 
     Equal shards: one all_gather_into_tensor straight into the result.
     Uneven shards: the local shard is copied into its rows of the result and
     every rank's rows are broadcast from their owner (NCCL over NVLink on
     GPUs, gloo on CPU), so no padded copies are made: the result (or ``out``)
-    is the only extra buffer.
+    is the only extra buffer.  With ``timeout_s`` the collectives are issued
+    asynchronously and waited for with that deadline (``wait_bounded``).
     """
     import torch.distributed as dist
+
+    asy = timeout_s is not None
 
     world = len(bounds)
     rows = [r1 - r0 for r0, r1 in bounds]
     tail = tuple(local.shape[1:])
     total = sum(rows)
     full = out if out is not None else local.new_empty((total, *tail))
+    works = []
     if all(r == rows[0] for r in rows):
-        dist.all_gather_into_tensor(full, local.contiguous(), group=group)
-        return full
-    me = dist.get_rank(group) if group is not None else dist.get_rank()
-    offs = [sum(rows[:k]) for k in range(world)]
-    full[offs[me]: offs[me] + rows[me]].copy_(local)
-    for k in range(world):
-        if rows[k]:
-            src = dist.get_global_rank(group, k) if group is not None else k
-            dist.broadcast(full[offs[k]: offs[k] + rows[k]], src=src, group=group)
+        works.append(dist.all_gather_into_tensor(full, local.contiguous(), group=group, async_op=asy))
+    else:
+        me = dist.get_rank(group) if group is not None else dist.get_rank()
+        offs = [sum(rows[:k]) for k in range(world)]
+        full[offs[me]: offs[me] + rows[me]].copy_(local)
+        for k in range(world):
+            if rows[k]:
+                src = dist.get_global_rank(group, k) if group is not None else k
+                works.append(dist.broadcast(full[offs[k]: offs[k] + rows[k]], src=src, group=group, async_op=asy))
+    if asy:
+        wait_bounded(works, timeout_s, group, "row all-gather")
     return full
 
 
-def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: bool = False, group=None):
+def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: bool = False, group=None,
+                     members: Membership | None = None, step: int = 0, timeout_s: float | None = None):
     """This rank's rows of A @ B with the engine's CSR operator; with
-    ``gather=True`` the full C assembled on every rank."""
+    ``gather=True`` the full C assembled on every rank.  With ``members``
+    the step first checks (on the host, before any launch) that every other
+    rank is still in the job; ``timeout_s`` bounds the all-gather."""
     import spmm_npu
 
+    if members is not None:
+        members.enter(step)
     bounds = shard_bounds(rowptr, world)
     r0, r1 = bounds[rank]
     rp, c, v = shard_csr(rowptr, col, val, r0, r1)
@@ -87,4 +223,4 @@ def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: boo
     local = spmm_npu.spmm_csr(rp, c, v, dense, start)
     if not gather:
         return local, (r0, r1)
-    return allgather_rows(local, bounds, group), (0, rowptr.numel() - 1)
+    return allgather_rows(local, bounds, group, timeout_s=timeout_s), (0, rowptr.numel() - 1)

@@ -5,6 +5,7 @@ spmm_npu.spmm_csr as the local operator."""
 
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -88,3 +89,97 @@ def test_allgather_reassembles_full_product():
         for r in range(world):
             np.testing.assert_allclose(results[r], ref, rtol=0, atol=0)
             np.testing.assert_allclose(results[("even", r)], ref[: 2 * half], rtol=0, atol=0)
+
+
+# ---------------------------------------------------------------- failure handling
+
+def _leaver(rank, world, port, results):
+    """Step 0 with both ranks; then rank 1 leaves the job and rank 0 must
+    learn it on the host before entering step 1's collective."""
+    import torch.distributed as dist
+
+    from spmm_dist import Membership, RankDeparted, spmm_csr_sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    members = Membership.for_default_group(timeout_s=20.0)
+    w = workloads.make(3, scale=0.01)
+    try:
+        members.enter(0)
+        bounds = shard_bounds(w.rowptr, world)
+        rp, c, v = shard_csr(w.rowptr, w.col, w.val, *bounds[rank])
+        full = allgather_rows(torch.from_numpy(oracle.spmm_csr_f64(rp, c, v, w.B)), bounds, timeout_s=20.0)
+        results[("step0", rank)] = full.shape[0]
+        if rank == 1:
+            members.leave("test: leaving between steps")
+            results[("left", rank)] = True
+            return
+        t0 = time.monotonic()
+        try:
+            members.enter(1)
+            results[("step1", rank)] = "entered"
+        except RankDeparted as exc:
+            results[("step1", rank)] = (exc.ranks, exc.step, time.monotonic() - t0)
+    finally:
+        dist.destroy_process_group()
+
+
+def _silent(rank, world, port, results):
+    """Rank 1 passes the membership check of step 1 and then never joins the
+    collective (it stops between steps without telling anyone); rank 0's
+    all-gather must end at its deadline with CollectiveTimeout."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from spmm_dist import CollectiveTimeout, Membership
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=8))
+    members = Membership.for_default_group(timeout_s=20.0)
+    local = torch.full((16, 8), float(rank))
+    bounds = [(0, 16), (16, 32)]
+    members.enter(0)
+    allgather_rows(local, bounds, timeout_s=20.0)
+    members.enter(1)
+    if rank == 1:
+        results["silent"] = True
+        time.sleep(4.0)           # gone quiet: no collective
+        os._exit(0)               # leaves without destroying the group
+    t0 = time.monotonic()
+    try:
+        allgather_rows(local, bounds, timeout_s=1.5)
+        results["timeout"] = "completed"
+    except CollectiveTimeout as exc:
+        results["timeout"] = (str(exc), time.monotonic() - t0)
+    os._exit(0)
+
+
+def _run(target, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=target, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=timeout)
+            assert p.exitcode == 0, p.exitcode
+        return dict(results)
+
+
+def test_departed_rank_is_seen_before_the_next_collective():
+    res = _run(_leaver)
+    assert res[("step0", 0)] == res[("step0", 1)] > 0 and res[("left", 1)]
+    ranks, step, waited = res[("step1", 0)]
+    assert ranks == [1] and step == 1 and waited < 10.0
+
+
+def test_collective_wait_is_bounded():
+    res = _run(_silent)
+    assert res["silent"]
+    msg, waited = res["timeout"]
+    assert "did not complete within 1.5 s" in msg and 1.4 <= waited < 6.0
