@@ -101,23 +101,34 @@ __device__ __forceinline__ void mbar_arrive_cpasync(unsigned bar)
 {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
+// POLL = 0: try_wait (the thread may be suspended until the phase
+// completes); POLL = 1: test_wait (never suspends; a spin).
+template <int POLL>
 __device__ __forceinline__ bool mbar_test(unsigned bar, unsigned parity)
 {
     unsigned ok;
-    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}\n"
-                 : "=r"(ok)
-                 : "r"(bar), "r"(parity)
-                 : "memory");
+    if constexpr (POLL == 0)
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}\n"
+                     : "=r"(ok)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}\n"
+                     : "=r"(ok)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
     return ok != 0;
 }
 // Bounded wait for the phase of the given parity; false on expiry.
+template <int POLL>
 __device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity)
 {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test<POLL>(bar, parity)) return true;
     const long long t0 = clock64();
     for (long long i = 0; i < kTcSpin; ++i) {
-        if (mbar_test(bar, parity)) return true;
+        if (mbar_test<POLL>(bar, parity)) return true;
         if (clock64() - t0 > kTcCycles) break;
     }
     return false;
@@ -183,7 +194,7 @@ __device__ __forceinline__ unsigned a_offset(int k, int j)
 // the V tile: [row group][entry group][8 entries x 16 bytes].
 __device__ __forceinline__ unsigned v_offset(int k, int g) { return (unsigned)(g * 256 + (k >> 3) * 128 + (k & 7) * 16); }
 
-template <typename I, int STAGES, int MINB>
+template <typename I, int STAGES, int MINB, int POLL>
 __global__ void __launch_bounds__(kTcThreads, MINB)
 window_tc_kernel(const WindowArgs a, int nslices)
 {
@@ -192,7 +203,7 @@ window_tc_kernel(const WindowArgs a, int nslices)
     const unsigned raw = (unsigned)__cvta_generic_to_shared(tc_smem_raw);
     const unsigned sbase = (raw + 1023u) & ~1023u;   // the A tiles need 1024-byte alignment
     unsigned char *gbase = tc_smem_raw + (sbase - raw);
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     int *s_col = reinterpret_cast<int *>(gbase + L::kColOff);
     unsigned short *s_val = reinterpret_cast<unsigned short *>(gbase + L::kValOff);
@@ -247,29 +258,34 @@ window_tc_kernel(const WindowArgs a, int nslices)
         *s_abort = 1;
     };
 
-    // Thread 0: MMAs for chunks [gmma, upto).
+    // Warp 0, converged: MMAs for chunks [gmma, upto), issued by lane 0.
     auto mma_until = [&](uint32_t upto) {
-        while (gmma < upto && !fail) {
+        while (gmma < upto) {
             const int st = (int)(gmma % STAGES);
-            if (!mbar_wait(bar_full + 8 * st, (gmma / STAGES) & 1u)) {
-                give_up(gmma);
+            const bool ok = !fail && mbar_wait<POLL>(bar_full + 8 * st, (gmma / STAGES) & 1u);
+            if (!ok) give_up(gmma);
+            if (!__all_sync(0xffffffffu, ok)) {
+                fail = true;
                 break;
             }
             tc_fence_after();
-            const unsigned meta = s_stage_meta[st];
-            const unsigned acc = meta & 0xffu, first = (meta >> 8) & 1u, last = (meta >> 9) & 1u;
-            const uint64_t ad = smem_desc(sbase + L::kAOff + st * L::kA, 2048, 1024, 2);
-            const uint64_t bd = smem_desc(sbase + L::kVOff + st * L::kV, 128, 256, 0);
-            tc_mma(tmem + acc * 16, ad, bd, kTcIdesc, first ? 0u : 1u);
-            tc_commit(bar_empty + 8 * st);
-            if (last) tc_commit(bar_acc + 8 * acc);
+            if (lane == 0) {
+                const unsigned meta = s_stage_meta[st];
+                const unsigned acc = meta & 0xffu, first = (meta >> 8) & 1u, last = (meta >> 9) & 1u;
+                const uint64_t ad = smem_desc(sbase + L::kAOff + st * L::kA, 2048, 1024, 2);
+                const uint64_t bd = smem_desc(sbase + L::kVOff + st * L::kV, 128, 256, 0);
+                tc_mma(tmem + acc * 16, ad, bd, kTcIdesc, first ? 0u : 1u);
+                tc_commit(bar_empty + 8 * st);
+                if (last) tc_commit(bar_acc + 8 * acc);
+            }
+            __syncwarp();
             ++gmma;
         }
     };
     // All threads: the pending item's rows from TMEM to C.
     auto epilogue = [&](int64_t item, uint32_t seq) {
         const unsigned acc = seq % kTcAcc;
-        const bool ok = !fail && mbar_wait(bar_acc + 8 * acc, (seq / kTcAcc) & 1u);
+        const bool ok = !fail && mbar_wait<POLL>(bar_acc + 8 * acc, (seq / kTcAcc) & 1u);
         if (!ok) give_up(item);
         __syncwarp();
         if (!__all_sync(0xffffffffu, ok)) return;   // tcgen05.ld is warp-collective
@@ -284,43 +300,41 @@ window_tc_kernel(const WindowArgs a, int nslices)
         for (int r = 0; r < 16; ++r) __stcs(o + r * a.N, __float2half_rn(v[r]));
     };
 
-    long long *s_meta = reinterpret_cast<long long *>(gbase + L::kMetaOff);   // cb, nb, vb, nv
-    const long long *vrs = s_meta + 8;                                         // vptr[16 s + r], r = 0..16
+    long long *s_meta = reinterpret_cast<long long *>(gbase + L::kMetaOff);
+    const volatile long long *vrs = s_meta + 8;                                // vptr[16 s + r], r = 0..16
     const int64_t nitems = a.nwin * nslices;
     for (int64_t it = blockIdx.x; it < nitems && !abort; it += gridDim.x) {
         const int64_t s = it / nslices;
         const int f0 = (int)(it % nslices) * kTcFW;
-        // ---- the window's stream: blocks [cb, cb + nb), CSR entries [vb, vb + nv)
-        __syncthreads();   // every read of the previous item's metadata is done
+        // ---- the window's stream: blocks [cb, cb + nb), CSR entries [vb, vb + nv);
+        // every thread reads the four bounds itself (broadcast loads), the 17
+        // row pointers go to shared memory for the CSR rows of the entries
+        __syncthreads();   // every read of the previous item's row pointers is done
         if (tid < 17) {
             int64_t vr = 0;
             if (a.vrows > 0 && 16 * s < a.vrows) vr = ld_idx(vptr + min(16 * s + tid, a.vrows));
             s_meta[8 + tid] = vr;
         }
-        if (tid == 32) {
-            int64_t cb = ld_idx(cptr + s), ce = ld_idx(cptr + s + 1);
-            if (cb < 0 || ce < cb || ce > a.nblocks) {
-                raise_status(a.status, SPMM_DEV_BAD_ROWPTR, s);
-                cb = ce = 0;
-            }
-            s_meta[0] = cb;
-            s_meta[1] = ce - cb;
+        int64_t cb = ld_idx(cptr + s), ce = ld_idx(cptr + s + 1);
+        if (cb < 0 || ce < cb || ce > a.nblocks) {
+            if (tid == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, s);
+            cb = ce = 0;
+        }
+        int64_t vb = 0, ve = 0;
+        if (a.vrows > 0 && 16 * s < a.vrows) {
+            vb = ld_idx(vptr + 16 * s);
+            ve = ld_idx(vptr + min(16 * s + 16, a.vrows));
         }
         __syncthreads();
-        if (tid == 0) {
-            int64_t vb = vrs[0], ve = vrs[16];
-            bool bad = vb < 0 || ve > a.vnnz;
+        {
+            bool bad = vb < 0 || ve < vb || ve > a.vnnz;
             for (int r = 0; r < 16; ++r) bad = bad || vrs[r + 1] < vrs[r];
             if (bad) {
-                raise_status(a.status, SPMM_DEV_BAD_ROWPTR, 16 * s);
+                if (tid == 0) raise_status(a.status, SPMM_DEV_BAD_ROWPTR, 16 * s);
                 vb = ve = 0;
             }
-            s_meta[2] = vb;
-            s_meta[3] = ve - vb;
         }
-        __syncthreads();
-        const int64_t cb = s_meta[0], vb = s_meta[2];
-        const int nb = (int)s_meta[1], nv = (int)s_meta[3];
+        const int nb = (int)(ce - cb), nv = (int)(ve - vb);
         const int nbc = (nb + 15) >> 4, nvc = (nv + 15) >> 4;
         const int nch = max(1, nbc + nvc);
         const uint32_t acc = gitem % kTcAcc;
@@ -367,7 +381,7 @@ window_tc_kernel(const WindowArgs a, int nslices)
             const int xend = min(nch, x0 + kTcSeg);
             for (int x = x0; x < xend; ++x) {
                 const int st = (int)(gchunk % STAGES);
-                if (!fail && !mbar_wait(bar_empty + 8 * st, ((gchunk / STAGES) & 1u) ^ 1u)) give_up(gchunk);
+                if (!fail && !mbar_wait<POLL>(bar_empty + 8 * st, ((gchunk / STAGES) & 1u) ^ 1u)) give_up(gchunk);
                 const unsigned As = sbase + L::kAOff + st * L::kA;
                 const unsigned Vs = sbase + L::kVOff + st * L::kV;
                 const int lx = x - x0;
@@ -402,18 +416,20 @@ window_tc_kernel(const WindowArgs a, int nslices)
                         }
                     }
                     if (tid == 0) s_stage_meta[st] = acc | (x == 0 ? 1u << 8 : 0u) | (x == nch - 1 ? 1u << 9 : 0u);
-                    fence_async_smem();   // this thread's st.shared precede the tensor core's reads
+                    // the value tile of a CSR chunk was written by st.shared: order it
+                    // before the tensor core's (async-proxy) reads
+                    if (tid < 32 && x >= nbc) fence_async_smem();
                     mbar_arrive_cpasync(bar_full + 8 * st);
                     mbar_arrive(bar_full + 8 * st);
                 }
                 ++gchunk;
-                if (tid == 0 && gchunk > (uint32_t)(STAGES - 2)) mma_until(gchunk - (STAGES - 2));
+                if (warp == 0 && gchunk > (uint32_t)(STAGES - 2)) mma_until(gchunk - (STAGES - 2));
             }
         }
         if (abort) break;
         // ---- the previous item is complete once its MMAs are: write it out
         if (prev_item >= 0) {
-            if (tid == 0) mma_until(prev_last);
+            if (warp == 0) mma_until(prev_last);
             epilogue(prev_item, gitem - 1);
             tc_fence_before();
             __syncthreads();   // every thread has read the accumulator before it is overwritten
@@ -426,14 +442,15 @@ window_tc_kernel(const WindowArgs a, int nslices)
     }
     // ---- drain: the last item's MMAs and epilogue
     if (!abort && prev_item >= 0) {
-        if (tid == 0) mma_until(prev_last);
+        if (warp == 0) mma_until(prev_last);
         epilogue(prev_item, gitem - 1);
     }
     asm volatile("cp.async.wait_all;\n" ::: "memory");
-    if (tid == 0 && gmma > 0) {
+    if (warp == 0 && gmma > 0) {
         // every MMA issued has completed before TMEM is released (bounded)
-        tc_commit(bar_done);
-        mbar_wait(bar_done, 0);
+        if (lane == 0) tc_commit(bar_done);
+        __syncwarp();
+        mbar_wait<POLL>(bar_done, 0);
     }
     tc_fence_before();
     __syncthreads();
@@ -443,17 +460,22 @@ window_tc_kernel(const WindowArgs a, int nslices)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTcCols) : "memory");
 }
 
-template <typename I, int STAGES>
+template <typename I, int STAGES, int POLL>
 cudaError_t launch_tc(const WindowArgs &a, cudaStream_t stream)
 {
     using L = TcShape<STAGES>;
     constexpr int MINB = 4;
-    auto kern = window_tc_kernel<I, STAGES, MINB>;
+    auto kern = window_tc_kernel<I, STAGES, MINB, POLL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return e;
+    // all of the unified L1/shared array as shared memory, so several CTAs fit
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTcThreads, L::kBytes);
     if (e != cudaSuccess) return e;
+    // SPMM_B200_TC_CTAS=n asks for n resident CTAs per SM (measurement)
+    if (const char *v = getenv("SPMM_B200_TC_CTAS")) per_sm = atoi(v);
     per_sm = std::min(std::max(per_sm, 1), 512 / kTcCols);   // TMEM columns of one SM
     const int nslices = (int)(a.N / kTcFW);
     const int64_t items = a.nwin * nslices;
@@ -474,7 +496,13 @@ bool window_tc_eligible(const WindowArgs &a, int dtype)
 cudaError_t launch_window_tc(const WindowArgs &a, int itype, cudaStream_t stream)
 {
     if (a.nwin <= 0) return cudaSuccess;
-    return itype == SPMM_I32 ? launch_tc<int, 8>(a, stream) : launch_tc<int64_t, 8>(a, stream);
+    // SPMM_B200_TC_POLL=spin selects the test_wait polling variant (measurement)
+    static const bool spin = [] {
+        const char *v = getenv("SPMM_B200_TC_POLL");
+        return v && strcmp(v, "spin") == 0;
+    }();
+    if (spin) return itype == SPMM_I32 ? launch_tc<int, 8, 1>(a, stream) : launch_tc<int64_t, 8, 1>(a, stream);
+    return itype == SPMM_I32 ? launch_tc<int, 8, 0>(a, stream) : launch_tc<int64_t, 8, 0>(a, stream);
 }
 
 }  // namespace spmmb

@@ -98,3 +98,10 @@ def test_bench_defaults_are_the_headline():
     a = bench.parse_args([])
     assert (a.config, a.scaling, a.op, a.gpus) == (5, "strong", "csr", 1)
     assert a.warmup >= 3
+
+
+def test_kernel_names_from_the_trace():
+    bench = load_bench()
+    assert bench.short_name("void spmmb::(anonymous namespace)::csr_ring_kernel<__half, int, 32, 4, 2, 2, true>"
+                            "(spmmb::GatherArgs)") == "csr_ring_kernel<__half, int, 32, 4, 2, 2, true>"
+    assert bench.short_name("void unnamed>::csr_fixup_kernel<__half, int>(GatherArgs)") == "csr_fixup_kernel<__half, int>"
