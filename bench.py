@@ -610,10 +610,23 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     one copy) used alternately: step i+1's host-to-device copy overlaps step
     i's kernel and its device-to-host copy of C; the kernel of step i+1 waits
     for its inputs and for C of step i to have been read back.  With one
-    device input set the copy of step i+1 waits for the kernel of step i."""
+    device input set the copy of step i+1 waits for the kernel of step i.
+
+    With several ranks, B (the last input, the same on every rank) crosses
+    the host link once per step for the whole job: each rank uploads its
+    1/N row block and an NCCL all-gather over NVLink assembles B on every
+    GPU (in place), inside the timed step."""
     import psutil
 
-    host_bytes = sum(t.numel() * t.element_size() for t in inputs)
+    import torch.distributed as dist
+
+    B = inputs[-1]
+    rank = dist.get_rank() if world > 1 else 0
+    shard_b = world > 1 and B.shape[0] % world == 0
+    kb = B.shape[0] // world if shard_b else B.shape[0]
+    b_rows = slice(rank * kb, (rank + 1) * kb) if shard_b else slice(0, B.shape[0])
+    host_bytes = sum(t.numel() * t.element_size() for t in inputs[:-1]) + \
+        B[b_rows].numel() * B.element_size()
     y0 = op(inputs)
     torch.cuda.synchronize()
     out_bytes = y0.numel() * y0.element_size()
@@ -632,12 +645,13 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
         h.copy_(t)
         return h
 
-    h_in = [pinned_copy(t) for t in inputs]
+    h_in = [pinned_copy(t) for t in inputs[:-1]] + [pinned_copy(B[b_rows])]
     h_out = torch.empty(y0.shape, dtype=y0.dtype, pin_memory=True)
     del y0
     torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info(dev)
-    two = allreduce(1.0 if free > host_bytes + 2 * out_bytes + (4 << 30) else 0.0, world, "min") >= 1.0
+    set_bytes = sum(t.numel() * t.element_size() for t in inputs)
+    two = allreduce(1.0 if free > set_bytes + 2 * out_bytes + (4 << 30) else 0.0, world, "min") >= 1.0
     sets = [inputs] + ([[torch.empty_like(t) for t in inputs]] if two else [])
     nset = len(sets)
     s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -651,8 +665,12 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
         with torch.cuda.stream(s_in):
             if state["used"][k]:
                 s_in.wait_event(comp_done[k])    # the last kernel that read set k is done
-            for d, h in zip(sets[k], h_in):
+            for d, h in zip(sets[k][:-1], h_in[:-1]):
                 d.copy_(h, non_blocking=True)
+            Bd = sets[k][-1]
+            Bd[b_rows].copy_(h_in[-1], non_blocking=True)
+            if shard_b:   # every rank's block to every GPU, over NVLink (in place)
+                dist.all_gather_into_tensor(Bd, Bd[b_rows])
             in_done[k].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_done[k])
@@ -699,7 +717,9 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     return {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps, "ms_per_step": round(e2e_ms / args.e2e_steps, 2),
             "pipeline": f"pinned host buffers, {nset} device input set(s): H2D of step i+1 overlaps "
-                        f"{'the kernel and ' if nset == 2 else ''}D2H of step i"}
+                        f"{'the kernel and ' if nset == 2 else ''}D2H of step i"
+                        + (f"; B uploaded as {world} row blocks (one per rank) and all-gathered over NCCL"
+                           if shard_b else "")}
 
 
 def run_preprocess_only(args, rank, world, local):
