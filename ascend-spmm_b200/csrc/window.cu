@@ -390,19 +390,17 @@ cudaError_t launch_f32(const WindowArgs &a, cudaStream_t stream)
 
 }  // namespace
 
-// Window kernel choice: SPMM_B200_WINDOW = block (block-synchronous
-// window.cu kernels), warp (window_warp.cu) or tc (tcgen05, window_tc.cu);
-// the default is the warp-pipelined kernel where eligible.
+// Window kernel choice, read at every launch: SPMM_B200_WINDOW = block
+// (block-synchronous window.cu kernels), warp (window_warp.cu) or tc
+// (tcgen05, window_tc.cu); the default is the warp-pipelined kernel where
+// eligible.
 int window_kernel_choice()
 {
-    static const int choice = [] {
-        const char *v = getenv("SPMM_B200_WINDOW");
-        if (v && strcmp(v, "block") == 0) return 1;
-        if (v && strcmp(v, "tc") == 0) return 2;
-        if (getenv("SPMM_B200_WINDOW_BLOCK")) return 1;
-        return 0;
-    }();
-    return choice;
+    const char *v = getenv("SPMM_B200_WINDOW");
+    if (v && strcmp(v, "block") == 0) return 1;
+    if (v && strcmp(v, "tc") == 0) return 2;
+    if (getenv("SPMM_B200_WINDOW_BLOCK")) return 1;
+    return 0;
 }
 
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined, cudaStream_t stream)

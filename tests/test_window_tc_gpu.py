@@ -1,6 +1,6 @@
 """The tcgen05 window kernel (window_tc.cu: TMEM accumulators, fp16, 128-feature
 slices) against the float64 oracle: every mixed-operator test module is rerun
-in a child process with SPMM_B200_WINDOW=tc (read once per process), so the
+in a child process with SPMM_B200_WINDOW=tc, so the
 golden layouts of the reference, random windows, graph layouts, spmm_cube and
 tile consumers, config-shaped matrices and B offsets beyond 2^32 elements all
 go through it wherever the width is a multiple of 128 (other widths keep the
