@@ -127,6 +127,11 @@ class Membership:
 
     def enter(self, step: int) -> None:
         self.store.set(self._key("ready", step, self.rank), "1")
+        if step >= 2:   # every rank passed step - 1, so nobody reads step - 2's keys any more
+            try:
+                self.store.delete_key(self._key("ready", step - 2, self.rank))
+            except Exception:   # stores without deletion keep the key
+                pass
         pending = {r for r in range(self.world) if r != self.rank}
         deadline = time.monotonic() + self.timeout_s
         while pending:

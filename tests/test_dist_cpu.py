@@ -183,3 +183,20 @@ def test_collective_wait_is_bounded():
     assert res["silent"]
     msg, waited = res["timeout"]
     assert "did not complete within 1.5 s" in msg and 1.4 <= waited < 6.0
+
+
+def test_membership_keys_do_not_accumulate():
+    """Each rank removes its step key two steps later (single-process store)."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from spmm_dist import Membership
+
+    store = dist.HashStore()
+    store.set_timeout(timedelta(seconds=5))
+    m = Membership(store, rank=0, world=1, timeout_s=1.0)
+    for step in range(6):
+        m.enter(step)
+    assert store.check(["spmm_dist/ready/5/0"]) and store.check(["spmm_dist/ready/4/0"])
+    assert not store.check(["spmm_dist/ready/3/0"]) and not store.check(["spmm_dist/ready/0/0"])
