@@ -24,6 +24,8 @@
 //    a stmatrix.trans transpose as 16-byte row segments.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
 #include "../../include/spmm_b200.h"
 #include "common.cuh"
@@ -575,6 +577,36 @@ bool window_warp_eligible(const WindowArgs &a, int dtype)
            al(a.out);
 }
 
+// Launch shape for measurement, read at every launch: SPMM_B200_WW =
+// <FW>s<stages>w<warps per CTA>.  The default (128 or 64 features, 3
+// stages, 4 warps, 3 or 5 CTAs per SM) measured fastest on configs 2 and 3.
+static int ww_variant()
+{
+    const char *e = getenv("SPMM_B200_WW");
+    if (!e) return 0;
+    static const char *const names[] = {"", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4"};
+    for (int i = 1; i < (int)(sizeof(names) / sizeof(names[0])); ++i)
+        if (strcmp(e, names[i]) == 0) return i;
+    return 0;
+}
+
+template <typename I>
+cudaError_t launch_ww_f16(const WindowArgs &a, cudaStream_t stream)
+{
+    const bool w128 = a.N % 128 == 0;
+    switch (ww_variant()) {
+    case 1: if (w128) return launch_ww<I, 128, 4, 2>(a, stream); break;
+    case 2: if (w128) return launch_ww<I, 128, 5, 2>(a, stream); break;
+    case 3: if (w128) return launch_ww<I, 128, 6, 2>(a, stream); break;
+    case 4: if (w128) return launch_ww<I, 128, 5, 1>(a, stream); break;
+    case 5: return launch_ww<I, 64, 6, 2>(a, stream);
+    case 6: return launch_ww<I, 64, 5, 4>(a, stream);
+    case 7: if (w128) return launch_ww<I, 128, 4, 4>(a, stream); break;
+    default: break;
+    }
+    return w128 ? launch_ww<I, 128, 3, 4>(a, stream) : launch_ww<I, 64, 3, 4>(a, stream);
+}
+
 cudaError_t launch_window_warp(const WindowArgs &a, int itype, int dtype, cudaStream_t stream)
 {
     if (a.nwin <= 0) return cudaSuccess;
@@ -582,9 +614,7 @@ cudaError_t launch_window_warp(const WindowArgs &a, int itype, int dtype, cudaSt
     // fit only 8 and measured 3 % slower on config 4, 4 stages 14 % slower)
     if (dtype == SPMM_F32)
         return itype == SPMM_I32 ? launch_ww_f32<int, 2, 2>(a, stream) : launch_ww_f32<int64_t, 2, 2>(a, stream);
-    if (a.N % 128 == 0)
-        return itype == SPMM_I32 ? launch_ww<int, 128, 3, 4>(a, stream) : launch_ww<int64_t, 128, 3, 4>(a, stream);
-    return itype == SPMM_I32 ? launch_ww<int, 64, 3, 4>(a, stream) : launch_ww<int64_t, 64, 3, 4>(a, stream);
+    return itype == SPMM_I32 ? launch_ww_f16<int>(a, stream) : launch_ww_f16<int64_t>(a, stream);
 }
 
 }  // namespace spmmb

@@ -76,7 +76,7 @@ def parse_args(argv=None):
     p.add_argument("--scale", type=float, default=1.0)
     p.add_argument("--op", choices=("csr", "mixed", "preprocess"), default="csr")
     p.add_argument("--scaling", choices=("strong", "weak"), default="strong")
-    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=8)
     p.add_argument("--preprocess-config", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -607,10 +607,13 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
 
     One pinned host set (config 5: 37 GB of inputs, 34 GB of output) and,
     device memory permitting, two device input sets (the resident tensors and
-    one copy) used alternately: step i+1's host-to-device copy overlaps step
-    i's kernel and its device-to-host copy of C; the kernel of step i+1 waits
-    for its inputs and for C of step i to have been read back.  With one
-    device input set the copy of step i+1 waits for the kernel of step i.
+    one copy) and two device outputs, used alternately: step i+1's
+    host-to-device copy overlaps step i's kernel and its device-to-host copy
+    of C, and the kernel of step i+1 waits only for its inputs and for the
+    read-back of C of step i-1 (whose output block it reuses), so in steady
+    state a step costs the slower of the two host-link directions.  With one
+    device input set the copy of step i+1 waits for the kernel of step i and
+    the kernel waits for the read-back of step i.
 
     With several ranks, B (the last input, the same on every rank) crosses
     the host link once per step for the whole job: each rank uploads its
@@ -654,14 +657,16 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     two = allreduce(1.0 if free > set_bytes + 2 * out_bytes + (4 << 30) else 0.0, world, "min") >= 1.0
     sets = [inputs] + ([[torch.empty_like(t) for t in inputs]] if two else [])
     nset = len(sets)
+    nout = nset    # one output per input set: the kernel of step i+1 never waits on the D2H of step i
     s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     in_done = [torch.cuda.Event() for _ in range(nset)]
     comp_done = [torch.cuda.Event() for _ in range(nset)]
-    d2h_done = torch.cuda.Event()
-    state = {"y": None, "step": 0, "used": [False] * nset}
+    d2h_done = [torch.cuda.Event() for _ in range(nout)]
+    state = {"y": [None] * nout, "step": 0, "used": [False] * nset, "out_used": [False] * nout}
 
     def e2e_step():
         k = state["step"] % nset
+        o = state["step"] % nout
         with torch.cuda.stream(s_in):
             if state["used"][k]:
                 s_in.wait_event(comp_done[k])    # the last kernel that read set k is done
@@ -674,16 +679,17 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
             in_done[k].record(s_in)
         with torch.cuda.stream(s_comp):
             s_comp.wait_event(in_done[k])
-            if state["step"] > 0:
-                s_comp.wait_event(d2h_done)      # the previous result has been read back
-            state["y"] = None                    # its block may now be handed out again on s_comp
-            state["y"] = op(sets[k])
+            if state["out_used"][o]:
+                s_comp.wait_event(d2h_done[o])   # the result held in slot o has been read back
+            state["y"][o] = None                 # its block may now be handed out again on s_comp
+            state["y"][o] = op(sets[k])
             comp_done[k].record(s_comp)
         with torch.cuda.stream(s_out):
             s_out.wait_event(comp_done[k])
-            h_out.copy_(state["y"], non_blocking=True)
-            d2h_done.record(s_out)
+            h_out.copy_(state["y"][o], non_blocking=True)
+            d2h_done[o].record(s_out)
         state["used"][k] = True
+        state["out_used"][o] = True
         state["step"] += 1
 
     e2e_step()
@@ -706,7 +712,7 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     h2d = allreduce(float(host_bytes), world, "sum")
     d2h = allreduce(float(out_bytes), world, "sum")
     # the host copy of the last step equals a resident run (compared in slabs)
-    state["y"] = None
+    state["y"] = [None] * nout
     del sets[1:]
     ref = op(inputs)
     torch.cuda.synchronize()
@@ -716,7 +722,7 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     del ref, h_in, h_out
     return {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps, "ms_per_step": round(e2e_ms / args.e2e_steps, 2),
-            "pipeline": f"pinned host buffers, {nset} device input set(s): H2D of step i+1 overlaps "
+            "pipeline": f"pinned host buffers, {nset} device input set(s) and output(s): H2D of step i+1 overlaps "
                         f"{'the kernel and ' if nset == 2 else ''}D2H of step i"
                         + (f"; B uploaded as {world} row blocks (one per rank) and all-gathered over NCCL"
                            if shard_b else "")}
