@@ -85,12 +85,14 @@ namespace {
 
 int csr_impl(const void *rowptr, const void *col, const void *value, const void *dense, void *out,
              int64_t M, int64_t K, int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
-             size_t workspace_bytes, void *stream, int batch_depth, const char *op)
+             size_t workspace_bytes, void *stream, int batch_depth, const char *op, void *out_mc = nullptr)
 {
     int rc = spmmb::check_csr_args(rowptr, col, value, dense, out, M, K, N, nnz, itype, dtype, op);
     if (rc || M == 0) return rc;
     if (misaligned(workspace))
         return set_error(SPMM_ERR_ARG, "%s: workspace must be 16-byte aligned", op);
+    if (misaligned(out_mc))
+        return set_error(SPMM_ERR_ARG, "%s: the multicast address must be 16-byte aligned", op);
     const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype);
     if (workspace_bytes < plan.workspace_bytes() || !workspace)
         return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
@@ -103,6 +105,7 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     a.M = M; a.K = K; a.N = N; a.nnz = nnz; a.row_begin = 0;
     a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
     spmmb::set_workspace(a, plan, workspace);
+    a.out_mc = out_mc;
     a.status = st;
     e = spmmb::launch_gather(a, itype, dtype, batch_depth, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, op);
@@ -164,9 +167,17 @@ cudaError_t side_stream(SideStream **out)
     return cudaSuccess;
 }
 
-size_t mixed_workspace(int64_t v_nnz, int64_t N, int dtype)
+// Workspace of the mixed operator: the window kernel's item schedule
+// (window_sched_bytes, when there are windows), then the CSR kernels'
+// scratch for the rows beyond the windows.
+size_t mixed_sched_bytes(int64_t n_windows, int64_t N)
 {
-    return spmmb::plan_gather(v_nnz, N, dtype).workspace_bytes();
+    return n_windows > 0 ? spmmb::window_sched_bytes(n_windows, N) : 0;
+}
+size_t mixed_workspace(int64_t n_windows, int64_t v_rows, int64_t v_nnz, int64_t N, int dtype)
+{
+    const size_t csr = v_rows > 16 * n_windows ? spmmb::plan_gather(v_nnz, N, dtype).workspace_bytes() : 0;
+    return mixed_sched_bytes(n_windows, N) + csr;
 }
 
 int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const void *Vrowptr,
@@ -186,7 +197,8 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
         return set_error(SPMM_ERR_ARG, "%s: null array", op);
     if (misaligned(dense) || misaligned(out) || misaligned(Cvalue) || misaligned(workspace))
         return set_error(SPMM_ERR_ARG, "%s: dense, Cvalue, out and workspace must be 16-byte aligned", op);
-    const size_t need = v_rows > 16 * n_windows ? mixed_workspace(v_nnz, N, dtype) : 0;
+    const size_t sched = mixed_sched_bytes(n_windows, N);
+    const size_t need = mixed_workspace(n_windows, v_rows, v_nnz, N, dtype);
     if (workspace_bytes < need || (need && !workspace))
         return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
                          workspace_bytes, need);
@@ -210,6 +222,7 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
         w.B = dense; w.out = out;
         w.nwin = n_windows; w.nblocks = n_blocks; w.vrows = v_rows; w.vnnz = v_nnz;
         w.K = K; w.N = N; w.status = st;
+        w.sched = sched ? workspace : nullptr;
         e = spmmb::launch_window(w, itype, dtype, pipelined, s);
         if (e != cudaSuccess) return cuda_error(e, op);
     }
@@ -219,7 +232,7 @@ int mixed_impl(const void *Crowptr, const void *Ccol, const void *Cvalue, const 
         a.rowptr = Vrowptr; a.col = Vcol; a.val = Vvalue; a.B = dense; a.out = out;
         a.M = v_rows; a.K = K; a.N = N; a.nnz = v_nnz; a.row_begin = 16 * n_windows;
         a.unit = plan.unit; a.unit_begin = plan.unit_begin; a.unit_end = plan.unit_end;
-        spmmb::set_workspace(a, plan, workspace);
+        spmmb::set_workspace(a, plan, static_cast<char *>(workspace) + sched);
         a.status = st;
         e = spmmb::launch_gather(a, itype, dtype, batch_depth, sg);
         if (both) {   // join even after a launch error, so s never races the side stream
@@ -289,6 +302,15 @@ int spmm_csr_launch(const void *rowptr, const void *col, const void *value, cons
                     stream, 0, "spmm_csr");
 }
 
+int spmm_csr_launch_multicast(const void *rowptr, const void *col, const void *value, const void *dense,
+                              void *out, void *out_multicast, int64_t M, int64_t K, int64_t N, int64_t nnz,
+                              int itype, int dtype, void *workspace, size_t workspace_bytes, void *stream)
+{
+    if (!out_multicast) return set_error(SPMM_ERR_ARG, "spmm_csr_multicast: null multicast address");
+    return csr_impl(rowptr, col, value, dense, out, M, K, N, nnz, itype, dtype, workspace, workspace_bytes,
+                    stream, 0, "spmm_csr_multicast", out_multicast);
+}
+
 int spmm_csr_aiv_mb_batch_launch(const void *rowptr, const void *col, const void *value, const void *dense,
                                  const int32_t *start, int64_t n_start, void *out, int64_t M, int64_t K,
                                  int64_t N, int64_t nnz, int itype, int dtype, void *workspace,
@@ -304,7 +326,7 @@ size_t spmm_ascend_cube_workspace_bytes(int64_t n_windows, int64_t n_blocks, int
                                         int64_t N, int dtype)
 {
     (void)n_blocks;
-    return v_rows > 16 * n_windows ? mixed_workspace(v_nnz, N, dtype) : 0;
+    return mixed_workspace(n_windows, v_rows, v_nnz, N, dtype);
 }
 
 #define SPMM_MIXED_ARGS                                                                                      \

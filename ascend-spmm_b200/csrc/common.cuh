@@ -22,6 +22,45 @@ __device__ __forceinline__ void raise_status(DevStatus *st, int code, long long 
                                                        (unsigned long long)detail);
 }
 
+// ---- stores of C --------------------------------------------------------
+
+// 16 bytes of C at p (an address inside `out`): a streaming store, or with a
+// multicast address `mc` for `out`, one multimem.st to the same offset
+// through it (NVLS: the switch writes every GPU's copy).  The bits are
+// stored as they are; the .f32 type only names the operand size.
+__device__ __forceinline__ void store_c16(void *out, void *mc, void *p, const uint4 &v)
+{
+    if (mc) {
+        char *q = static_cast<char *>(mc) + (static_cast<char *>(p) - static_cast<char *>(out));
+        asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(q),
+                     "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+                     "f"(__uint_as_float(v.w))
+                     : "memory");
+    } else {
+        __stcs(static_cast<uint4 *>(p), v);
+    }
+}
+
+// 8 bytes of C at p, as store_c16.
+__device__ __forceinline__ void store_c8(void *out, void *mc, void *p, const uint2 &v)
+{
+    if (mc) {
+        char *q = static_cast<char *>(mc) + (static_cast<char *>(p) - static_cast<char *>(out));
+        asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};\n" ::"l"(q), "f"(__uint_as_float(v.x)),
+                     "f"(__uint_as_float(v.y))
+                     : "memory");
+    } else {
+        *static_cast<uint2 *>(p) = v;
+    }
+}
+
+// After the last multicast store of a thread: orders its stores before any
+// later signal at system scope (the caller's cross-GPU barrier).
+__device__ __forceinline__ void release_c(const void *mc)
+{
+    if (mc) __threadfence_system();
+}
+
 // ---- element conversions ------------------------------------------------
 
 template <typename T> __device__ __forceinline__ float to_f32(T x);

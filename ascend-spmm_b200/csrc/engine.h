@@ -80,6 +80,11 @@ struct GatherArgs {
     // end (its tail partial was written), else -1; the fix-up then needs no
     // search for it.
     int64_t *split_rows;
+    // Optional NVLink multicast address of `out` (same layout): every row
+    // of C is then stored once through it with multimem.st, and the switch
+    // writes it into each GPU's copy bound to the multicast object; `out`
+    // itself is not written directly.  nullptr: plain stores to `out`.
+    void *out_mc;
 };
 
 // Points a's scratch arrays into a workspace of plan.workspace_bytes().
@@ -119,7 +124,14 @@ struct WindowArgs {
     int64_t K;
     int64_t N;
     DevStatus *status;
+    // Optional scratch of window_sched_bytes(nwin, N) bytes for the
+    // warp-pipelined kernels' item schedule (heavy items first, claimed
+    // dynamically); nullptr keeps the static item order.
+    void *sched;
 };
+
+// Bytes of WindowArgs::sched for nwin windows of width N (a multiple of 256).
+size_t window_sched_bytes(int64_t nwin, int64_t N);
 
 // pipelined: 1 = multi-stage block stream (default), 0 = single stage.
 cudaError_t launch_window(const WindowArgs &a, int itype, int dtype, int pipelined,

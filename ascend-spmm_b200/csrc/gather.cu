@@ -131,7 +131,7 @@ csr_gather_kernel(const GatherArgs a)
 #pragma unroll
                 for (int q = 0; q < VPL; ++q) {
                     const int vi = gl + q * G;
-                    if (vi < NV) __stcs(orow + vi, pack16<T>(acc[q]));
+                    if (vi < NV) store_c16(a.out, a.out_mc, orow + vi, pack16<T>(acc[q]));
                 }
             } else {
                 float *prow = a.partial + ((u - a.unit_begin) * 2 + (head ? 0 : 1)) * a.N;
@@ -147,6 +147,7 @@ csr_gather_kernel(const GatherArgs a)
             }
         }
     }
+    release_c(a.out_mc);   // multicast rows ordered before the caller's barrier
 }
 
 // ---------------------------------------------------------------------------
@@ -253,7 +254,7 @@ csr_stream_kernel(const GatherArgs a)
 #pragma unroll
             for (int q = 0; q < VPL; ++q) {
                 const int vi = gl + q * G;
-                if (vi < NV) __stcs(out + row * NV + vi, make_uint4(0, 0, 0, 0));
+                if (vi < NV) store_c16(a.out, a.out_mc, out + row * NV + vi, make_uint4(0, 0, 0, 0));
             }
         };
         for (; r < a.M; ++r) {
@@ -398,7 +399,7 @@ csr_stream_kernel(const GatherArgs a)
 #pragma unroll
                             for (int q = 0; q < VPL; ++q) {
                                 const int vi = gl + q * G;
-                                if (vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
+                                if (vi < NV) store_c16(a.out, a.out_mc, out + row * NV + vi, pack16<T>(acc[q]));
                             }
                         }
 #pragma unroll
@@ -415,6 +416,7 @@ csr_stream_kernel(const GatherArgs a)
             }
         }
     }
+    release_c(a.out_mc);   // multicast rows ordered before the caller's barrier
 }
 
 // ---------------------------------------------------------------------------
@@ -578,7 +580,7 @@ csr_ring_kernel(const GatherArgs a)
 #pragma unroll
             for (int q = 0; q < VPL; ++q) {
                 const int vi = gl + q * G;
-                if (FULL || vi < NV) __stcs(out + row * NV + vi, make_uint4(0, 0, 0, 0));
+                if (FULL || vi < NV) store_c16(a.out, a.out_mc, out + row * NV + vi, make_uint4(0, 0, 0, 0));
             }
         };
         // first row with a nonzero in the unit; the empty rows before it that
@@ -825,7 +827,7 @@ csr_ring_kernel(const GatherArgs a)
 #pragma unroll
                             for (int q = 0; q < VPL; ++q) {
                                 const int vi = gl + q * G;
-                                if (FULL || vi < NV) __stcs(out + row * NV + vi, pack16<T>(acc[q]));
+                                if (FULL || vi < NV) store_c16(a.out, a.out_mc, out + row * NV + vi, pack16<T>(acc[q]));
                             }
                         }
 #pragma unroll
@@ -848,6 +850,7 @@ csr_ring_kernel(const GatherArgs a)
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");
     }
+    release_c(a.out_mc);   // multicast rows ordered before the caller's barrier
 }
 
 
@@ -887,14 +890,16 @@ csr_fixup_kernel(const GatherArgs a)
             }
             T *o = static_cast<T *>(a.out) + r * a.N + f;
             if constexpr (sizeof(T) == 2) {
-                __half2 *o2 = reinterpret_cast<__half2 *>(o);
-                o2[0] = __floats2half2_rn(s.x, s.y);
-                o2[1] = __floats2half2_rn(s.z, s.w);
+                const __half2 lo = __floats2half2_rn(s.x, s.y), hi = __floats2half2_rn(s.z, s.w);
+                store_c8(a.out, a.out_mc, o,
+                         make_uint2(*reinterpret_cast<const unsigned *>(&lo), *reinterpret_cast<const unsigned *>(&hi)));
             } else {
-                *reinterpret_cast<float4 *>(o) = s;
+                store_c16(a.out, a.out_mc, o,
+                          make_uint4(__float_as_uint(s.x), __float_as_uint(s.y), __float_as_uint(s.z), __float_as_uint(s.w)));
             }
         }
     }
+    release_c(a.out_mc);   // multicast rows ordered before the caller's barrier
 }
 
 template <typename T, typename I>

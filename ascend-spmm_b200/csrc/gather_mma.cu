@@ -150,7 +150,7 @@ csr_mma_kernel(const GatherArgs a, int nslices)
             if (b1 == b0) {
                 uint4 *o = reinterpret_cast<uint4 *>(out + r * rowbytes + f0 * 2);
 #pragma unroll
-                for (int v = 0; v < PIECES; ++v) __stcs(o + v, make_uint4(0, 0, 0, 0));
+                for (int v = 0; v < PIECES; ++v) store_c16(a.out, a.out_mc, o + v, make_uint4(0, 0, 0, 0));
             }
         }
 
@@ -216,7 +216,7 @@ csr_mma_kernel(const GatherArgs a, int nslices)
                     const int n = idx / PIECES, v = idx % PIECES;
                     if ((dmask >> (4 * n)) & 1u) {
                         uint4 *o = reinterpret_cast<uint4 *>(out + (wbase + n) * rowbytes + f0 * 2) + v;
-                        __stcs(o, lds128(epi + (unsigned)(n * PITCH + v * 16)));
+                        store_c16(a.out, a.out_mc, o, lds128(epi + (unsigned)(n * PITCH + v * 16)));
                     }
                 }
                 __syncwarp();
@@ -381,6 +381,7 @@ csr_mma_kernel(const GatherArgs a, int nslices)
         __syncwarp();
         if (!ok) break;
     }
+    release_c(a.out_mc);   // multicast rows ordered before the caller's barrier
 }
 
 // unit_rows[k] = first row r in [row_begin, M] with rowptr[r] >= (unit_begin

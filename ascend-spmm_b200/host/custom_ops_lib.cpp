@@ -147,6 +147,43 @@ at::Tensor spmm_csr_impl(const at::Tensor &rowptr, const at::Tensor &col, const 
     return csr_op(rowptr, col, value, dense, start, "spmm_csr", false, &spmm_csr_launch);
 }
 
+// This rank's row shard of C written through an NVLink multicast address of
+// `out` (spmm_csr_launch_multicast): every GPU whose copy is bound to the
+// multicast object receives the rows.  `out` is this rank's rows of the
+// replicated C; `out_multicast` the multicast address of out's first byte.
+at::Tensor spmm_csr_multicast_impl(const at::Tensor &rowptr, const at::Tensor &col, const at::Tensor &value,
+                                   const at::Tensor &dense, const at::Tensor &out, int64_t out_multicast)
+{
+    const char *op = "spmm_csr_multicast";
+    TORCH_CHECK_CUDA(rowptr);
+    TORCH_CHECK_CUDA(col);
+    TORCH_CHECK_CUDA(value);
+    TORCH_CHECK_CUDA(dense);
+    TORCH_CHECK_CUDA(out);
+    TORCH_CHECK(rowptr.dim() == 1 && col.dim() == 1 && value.dim() == 1, op, ": rowptr, col and value must be 1-D");
+    TORCH_CHECK(dense.dim() == 2, op, ": dense must be two-dimensional");
+    check_dense_contract(dense, dense.scalar_type() == at::kHalf ? 16 : 8, op);
+    check_value_contract(value, dense, "value");
+    TORCH_CHECK(col.size(0) == value.size(0), op, ": col and value must have equal length");
+    TORCH_CHECK(rowptr.size(0) >= 1, op, ": rowptr must hold rows + 1 entries");
+    same_device({&rowptr, &col, &value, &out}, dense, op);
+    const int itype = index_code({&rowptr, &col}, op);
+    const int64_t rows = rowptr.size(0) - 1, D = dense.size(1), nnz = col.size(0);
+    TORCH_CHECK(out.scalar_type() == dense.scalar_type(), op, ": out must have the dtype of dense");
+    TORCH_CHECK(out.dim() == 2 && out.size(0) == rows && out.size(1) == D && out.is_contiguous(), op,
+                ": out must be a contiguous [rows, N] tensor");
+    TORCH_CHECK(out_multicast != 0 && out_multicast % 16 == 0, op, ": multicast address must be 16-byte aligned");
+    c10::cuda::CUDAGuard guard(dense.device());
+    const int dt = dtype_code(dense);
+    const size_t wbytes = spmm_csr_workspace_bytes(rows, D, nnz, dt);
+    at::Tensor ws = workspace(wbytes, dense);
+    const at::Tensor B = aligned16(dense);
+    check_rc(spmm_csr_launch_multicast(rowptr.data_ptr(), col.data_ptr(), value.data_ptr(), B.data_ptr(),
+                                       out.data_ptr(), reinterpret_cast<void *>(out_multicast), rows, dense.size(0),
+                                       D, nnz, itype, dt, ws.data_ptr(), wbytes, stream_of(dense)));
+    return out;
+}
+
 at::Tensor spmm_csr_aiv_mb_batch_impl(const at::Tensor &rowptr, const at::Tensor &col, const at::Tensor &value,
                                       const at::Tensor &dense, const at::Tensor &start)
 {
@@ -582,6 +619,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m)
 {
     m.def("spmm_csr", &spmm_csr_impl,
           "CUDA CSR SpMM; FP16 width divisible by 16 with MAXD=1024, FP32 width divisible by 8 with MAXD=512");
+    m.def("spmm_csr_multicast", &spmm_csr_multicast_impl,
+          "this rank's rows of A @ B stored through an NVLink multicast address of out (every bound copy)");
     m.def("spmm_cube", &spmm_cube_impl,
           "CUDA window SpMM over (column << 4 | row) entries; width divisible by 16, MAXD=1024 for FP16 and 512 "
           "for FP32");

@@ -5,9 +5,12 @@ same operator.  A is cut into contiguous row ranges balanced by nonzeros at
 16-row window boundaries (so window layouts built per shard keep whole
 windows), B is replicated on every GPU, and each rank computes its own rows
 with the single-GPU operators - there is no communication in the SpMM
-itself.  C stays row-sharded; ``allgather_rows`` assembles the full C over
-NCCL (one all-gather for equal shards, one broadcast per rank otherwise) only
-when a caller asks for it.
+itself.  C stays row-sharded; when a caller asks for the full C on every
+rank, ``MulticastRows`` fuses the gather into the SpMM (each finished row is
+stored once through an NVLink multicast address and the NVSwitch writes it
+into every GPU's copy while the kernel runs), and ``allgather_rows``
+assembles it over NCCL where multicast is not available (one all-gather for
+equal shards, one broadcast per rank otherwise).
 
 Failure handling (no GPU fault is involved in any of it): ``Membership``
 keeps the ranks' presence in the process group's store, so a rank that
@@ -211,12 +214,80 @@ def allgather_rows(local: torch.Tensor, bounds: list[tuple[int, int]], group=Non
     return full
 
 
+def group_barrier(group=None, timeout_s: float | None = None, device=None) -> None:
+    """Stream-ordered barrier: a one-element all-reduce on the current stream
+    (it completes on a rank only after every rank's earlier work on its own
+    stream), waited for with ``timeout_s`` when given."""
+    import torch.distributed as dist
+
+    flag = torch.zeros(1, device=device)
+    work = dist.all_reduce(flag, group=group, async_op=timeout_s is not None)
+    if timeout_s is not None:
+        wait_bounded([work], timeout_s, group, "barrier")
+
+
+class MulticastRows:
+    """The full C ([rows, N]) replicated on every rank of ``group`` in NVLink
+    multicast memory: one buffer per GPU from torch's symmetric memory, bound
+    by the CUDA driver into one multicast object (NVLS through the NVSwitch).
+
+    ``spmm_csr_sharded(..., gather=True, replica=this)`` runs the CSR kernels
+    with this rank's rows stored through the multicast address
+    (``custom_ops_lib.spmm_csr_multicast``): each finished row goes out once
+    and the switch writes it into every GPU's copy while the kernel runs, so
+    no separate all-gather pass follows.  Each call is bracketed by
+    stream-ordered barriers: the one before keeps a rank from overwriting
+    copies that another rank still reads from the previous call, the one
+    after completes every copy.  Raises ``RuntimeError`` where the group has
+    no multicast support (use ``allgather_rows`` there).
+    """
+
+    def __init__(self, rows: int, N: int, dtype, device, group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        grp = group if group is not None else dist.group.WORLD
+        self.group = group
+        try:
+            self.buf = symm.empty((rows, N), dtype=dtype, device=device)
+            self.handle = symm.rendezvous(self.buf, grp)
+            mc_base = int(self.handle.multicast_ptr)
+        except Exception as e:   # allocation or rendezvous refused by the runtime
+            raise RuntimeError(f"symmetric-memory replica unavailable: {e}") from e
+        if not mc_base:
+            raise RuntimeError("NVLink multicast (NVLS) is not available to this group")
+        # the multicast object binds each rank's buffer from its first byte;
+        # the replica must lie inside that buffer
+        base = int(self.handle.buffer_ptrs[self.handle.rank])
+        off = self.buf.data_ptr() - base
+        if off < 0 or off + self.buf.numel() * self.buf.element_size() > int(self.handle.buffer_size):
+            raise RuntimeError("replica lies outside its symmetric-memory buffer")
+        self.mc = mc_base + off
+        if self.mc % 16:
+            raise RuntimeError("multicast address of the replica is not 16-byte aligned")
+
+    def close(self) -> None:
+        """Drops the replica; call on every rank at the same point, after the
+        last step and before the process group is destroyed, so no rank's
+        copy leaves the multicast object while another still writes it."""
+        self.handle = None
+        self.buf = None
+
+    def rows_mc(self, r0: int) -> int:
+        """Multicast address of row ``r0`` of the replica."""
+        return self.mc + r0 * self.buf.shape[1] * self.buf.element_size()
+
+
 def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: bool = False, group=None,
-                     members: Membership | None = None, step: int = 0, timeout_s: float | None = None):
+                     members: Membership | None = None, step: int = 0, timeout_s: float | None = None,
+                     replica: MulticastRows | None = None):
     """This rank's rows of A @ B with the engine's CSR operator; with
-    ``gather=True`` the full C assembled on every rank.  With ``members``
-    the step first checks (on the host, before any launch) that every other
-    rank is still in the job; ``timeout_s`` bounds the all-gather."""
+    ``gather=True`` the full C on every rank: with ``replica`` (a
+    ``MulticastRows`` of C's shape) the rows are multicast by the SpMM
+    kernels themselves and ``replica.buf`` is returned, otherwise they are
+    all-gathered over NCCL afterwards.  With ``members`` the step first
+    checks (on the host, before any launch) that every other rank is still
+    in the job; ``timeout_s`` bounds the collectives."""
     import spmm_npu
 
     if members is not None:
@@ -224,8 +295,18 @@ def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: boo
     bounds = shard_bounds(rowptr, world)
     r0, r1 = bounds[rank]
     rp, c, v = shard_csr(rowptr, col, val, r0, r1)
+    M = rowptr.numel() - 1
+    if gather and replica is not None:
+        import custom_ops_lib
+
+        if tuple(replica.buf.shape) != (M, dense.shape[1]) or replica.buf.dtype != dense.dtype:
+            raise ValueError("replica must be a [rows, N] buffer of the dense operand's dtype")
+        group_barrier(group, timeout_s, dense.device)
+        custom_ops_lib.spmm_csr_multicast(rp, c, v, dense, replica.buf[r0:r1], replica.rows_mc(r0))
+        group_barrier(group, timeout_s, dense.device)
+        return replica.buf, (0, M)
     start = torch.zeros(40, dtype=torch.int32, device=dense.device)
     local = spmm_npu.spmm_csr(rp, c, v, dense, start)
     if not gather:
         return local, (r0, r1)
-    return allgather_rows(local, bounds, group, timeout_s=timeout_s), (0, rowptr.numel() - 1)
+    return allgather_rows(local, bounds, group, timeout_s=timeout_s), (0, M)

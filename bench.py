@@ -564,7 +564,10 @@ def run_ours(args, rank, world, local):
         gms = allreduce(g0.elapsed_time(g1), world, "max") / 3
         extra["allgather"] = {"ms": round(gms, 3), "bytes": int(full.numel() * full.element_size()),
                               "note": "optional full-C all-gather over NCCL, not part of value"}
-        del y, full
+        del y
+        extra["allgather"]["fused_multicast"] = fused_multicast_leg(rp, col, val, B, bounds, rank, world, dev,
+                                                                    full, stream)
+        del full
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         extra["cpu_baseline"] = cpu_baseline(w)
     if not args.no_e2e:
@@ -597,6 +600,55 @@ def run_ours(args, rank, world, local):
     }
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def fused_multicast_leg(rp, col, val, B, bounds, rank, world, dev, full_nccl, stream):
+    """The SpMM with the full-C gather fused into it: this rank's rows are
+    stored by the CSR kernels through the NVLink multicast address of a
+    symmetric-memory replica of C (``spmm_dist.MulticastRows``), between two
+    stream-ordered barriers.  Timed like the NCCL leg (3 calls, max over
+    ranks) and checked bit for bit against the NCCL all-gather result."""
+    import custom_ops_lib
+    from spmm_dist import MulticastRows, group_barrier
+
+    r0, r1 = bounds[rank]
+    rep, why = None, ""
+    torch.cuda.empty_cache()   # the replica comes from the driver, not from torch's cache
+    try:
+        rep = MulticastRows(full_nccl.shape[0], full_nccl.shape[1], full_nccl.dtype, dev)
+        ok = 1.0
+    except RuntimeError as e:
+        why, ok = str(e), 0.0
+    if allreduce(ok, world, "min") < 1.0:
+        if rep is not None:
+            rep.close()
+        barrier(world)
+        return {"unavailable": why if not ok else "multicast replica unavailable on another rank"}
+    out = rep.buf[r0:r1]
+
+    def fused():
+        group_barrier(device=dev)
+        custom_ops_lib.spmm_csr_multicast(rp, col, val, B, out, rep.rows_mc(r0))
+        group_barrier(device=dev)
+
+    fused()
+    torch.cuda.synchronize()
+    same = allreduce(1.0 if torch.equal(rep.buf, full_nccl) else 0.0, world, "min") >= 1.0
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(3):
+        fused()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    fms = allreduce(f0.elapsed_time(f1), world, "max") / 3
+    del out
+    barrier(world)     # no rank writes the replicas any more
+    rep.close()
+    torch.cuda.synchronize()
+    barrier(world)
+    return {"ms": round(fms, 3), "equal_to_nccl_gather": same,
+            "note": "SpMM + full-C replication in one kernel (multimem.st through NVSwitch), barriers included"}
 
 
 def run_e2e(args, w, inputs, op, dev, world, flops):

@@ -94,6 +94,23 @@ int spmm_csr_aiv_mb_batch_launch(const void *rowptr, const void *col, const void
                                  int itype, int dtype, void *workspace,
                                  size_t workspace_bytes, void *stream);
 
+/* Row-sharded CSR SpMM with the whole C replicated on every GPU of a job
+ * (one process per GPU, each multiplying its own row shard): as
+ * spmm_csr_launch, but every row of this call's C is stored once through
+ * `out_multicast`, an NVLink multicast (NVLS) address of `out` - the
+ * multicast object binds the same buffer of every GPU at the same offset -
+ * so the switch writes each row into all copies while the kernel runs; `out`
+ * itself receives the rows the same way.  The caller puts a cross-GPU
+ * barrier after the call before any GPU reads the copies.  No counterpart in
+ * the reference (a single-device operator): the multi-GPU form of
+ * spmm_csr_impl_npu (extension/custom_op.cpp:67-88) fused with the row all-gather
+ * that would follow it.  Same workspace as spmm_csr_launch; out_multicast
+ * 16-byte aligned. */
+int spmm_csr_launch_multicast(const void *rowptr, const void *col, const void *value,
+                              const void *dense, void *out, void *out_multicast, int64_t M,
+                              int64_t K, int64_t N, int64_t nnz, int itype, int dtype,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
 /* CSR SpMM for callers that cannot allocate device memory when they call
  * (for example a service binding this ABI through cgo/JNI/FFI with a device
  * memory budget fixed at start-up, or a latency-critical loop where a
@@ -121,6 +138,9 @@ int spmm_csr_launch_noalloc(const void *rowptr, const void *col, const void *val
 /*   Ccol_ids [n_blocks]       block column ids                             */
 /*   Cvalue   [16 * n_blocks]  Cvalue[16 b + i] = A[row i of window, col b] */
 /*   Vrowptr  [v_rows + 1], Vcol_ids [v_nnz], Vvalue [v_nnz]                */
+/* The workspace holds the window kernel's item schedule (heavy windows    */
+/* first, claimed dynamically; 8 bytes per window and 64-feature slice)    */
+/* and the scratch of the CSR rows beyond the windows.                     */
 /* ---------------------------------------------------------------------- */
 size_t spmm_ascend_cube_workspace_bytes(int64_t n_windows, int64_t n_blocks, int64_t v_rows,
                                         int64_t v_nnz, int64_t N, int dtype);
