@@ -77,6 +77,8 @@ def parse_args(argv=None):
     p.add_argument("--op", choices=("csr", "mixed", "preprocess"), default="csr")
     p.add_argument("--scaling", choices=("strong", "weak"), default="strong")
     p.add_argument("--e2e-steps", type=int, default=8)
+    p.add_argument("--e2e-outputs", type=int, choices=(1, 2), default=2,
+                   help="device outputs in the e2e pipeline (1: a step's kernel waits for the previous read-back)")
     p.add_argument("--preprocess-config", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -709,7 +711,7 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     two = allreduce(1.0 if free > set_bytes + 2 * out_bytes + (4 << 30) else 0.0, world, "min") >= 1.0
     sets = [inputs] + ([[torch.empty_like(t) for t in inputs]] if two else [])
     nset = len(sets)
-    nout = nset    # one output per input set: the kernel of step i+1 never waits on the D2H of step i
+    nout = min(nset, args.e2e_outputs)   # 2: the kernel of step i+1 never waits on the D2H of step i
     s_in, s_comp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     in_done = [torch.cuda.Event() for _ in range(nset)]
     comp_done = [torch.cuda.Event() for _ in range(nset)]
@@ -774,7 +776,7 @@ def run_e2e(args, w, inputs, op, dev, world, flops):
     del ref, h_in, h_out
     return {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "steps": args.e2e_steps, "ms_per_step": round(e2e_ms / args.e2e_steps, 2),
-            "pipeline": f"pinned host buffers, {nset} device input set(s) and output(s): H2D of step i+1 overlaps "
+            "pipeline": f"pinned host buffers, {nset} device input set(s), {nout} output(s): H2D of step i+1 overlaps "
                         f"{'the kernel and ' if nset == 2 else ''}D2H of step i"
                         + (f"; B uploaded as {world} row blocks (one per rank) and all-gathered over NCCL"
                            if shard_b else "")}
