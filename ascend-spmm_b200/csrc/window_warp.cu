@@ -237,6 +237,7 @@ window_warp_kernel(const WindowArgs a, int nslices)
     const char *B = static_cast<const char *>(a.B);
     char *out = static_cast<char *>(a.out);
     const int64_t rowbytes = a.N * 2;
+    const int rowb = (int)rowbytes;   // N <= 1024 (the operators' width contract)
 
     const int64_t nitems = a.nwin * nslices;
     // items: claimed from the schedule when there is one (the next claim is
@@ -256,6 +257,7 @@ window_warp_kernel(const WindowArgs a, int nslices)
         if (claim && lane == 0) np = atomicAdd(claim, 1ull);
         const int64_t s = it / nslices;
         const int f0 = (int)(it % nslices) * FW;
+        const char *Bf = B + f0 * 2 + (lane % PIECES) * 16;   // this lane's piece of B row 0's slice
 
         // ---- the window's stream: blocks [cb, cb + nb), CSR entries [vb, vb + nv)
         int64_t cb = ld_idx(cptr + s), ce = ld_idx(cptr + s + 1);
@@ -325,7 +327,7 @@ window_warp_kernel(const WindowArgs a, int nslices)
             for (int i = 0; i < 16 / RPI; ++i) {
                 const int kk = lane / PIECES + RPI * i;
                 const int ck = __shfl_sync(kFull, cc, kk);
-                const char *src = B + (int64_t)(ck >= 0 ? ck : 0) * rowbytes + f0 * 2 + v * 16;
+                const char *src = Bf + (int64_t)(ck >= 0 ? ck : 0) * rowb;   // 32 x 32 -> 64-bit multiply-add
                 cp16(st + (unsigned)(kk * PITCH + v * 16), src, ck >= 0 ? 16 : 0);
             }
             if (blk) {
@@ -729,7 +731,7 @@ static int ww_variant()
 {
     const char *e = getenv("SPMM_B200_WW");
     if (!e) return 0;
-    static const char *const names[] = {"", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4"};
+    static const char *const names[] = {"", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4", "64s3w4"};
     for (int i = 1; i < (int)(sizeof(names) / sizeof(names[0])); ++i)
         if (strcmp(e, names[i]) == 0) return i;
     return 0;
@@ -747,6 +749,7 @@ cudaError_t launch_ww_f16(const WindowArgs &a, cudaStream_t stream)
     case 5: return launch_ww<I, 64, 6, 2>(a, stream);
     case 6: return launch_ww<I, 64, 5, 4>(a, stream);
     case 7: if (w128) return launch_ww<I, 128, 4, 4>(a, stream); break;
+    case 8: return launch_ww<I, 64, 3, 4>(a, stream);
     default: break;
     }
     return w128 ? launch_ww<I, 128, 3, 4>(a, stream) : launch_ww<I, 64, 3, 4>(a, stream);
