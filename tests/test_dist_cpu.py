@@ -200,3 +200,19 @@ def test_membership_keys_do_not_accumulate():
         m.enter(step)
     assert store.check(["spmm_dist/ready/5/0"]) and store.check(["spmm_dist/ready/4/0"])
     assert not store.check(["spmm_dist/ready/3/0"]) and not store.check(["spmm_dist/ready/0/0"])
+
+
+def test_multicast_replica_refuses_cleanly_where_unavailable(tmp_path):
+    """Where the group cannot hold an NVLink multicast replica (here: CPU
+    tensors on a gloo group) MulticastRows raises RuntimeError, the signal
+    for callers to take the NCCL all-gather instead; nothing is left bound."""
+    import torch.distributed as dist
+
+    from spmm_dist import MulticastRows
+
+    dist.init_process_group("gloo", init_method=f"file://{tmp_path / 'store'}", rank=0, world_size=1)
+    try:
+        with pytest.raises(RuntimeError, match="replica unavailable|multicast"):
+            MulticastRows(32, 16, torch.float16, torch.device("cpu"))
+    finally:
+        dist.destroy_process_group()
