@@ -7,7 +7,7 @@
 // Cvalue[16b + i] * B[Ccol[b], :] plus the CSR entries of those rows, summed
 // in fp32 and rounded once.
 //
-// Design: a warp owns (window, feature slice of FW = 64 or 128 features) and
+// Design: a warp owns (window, feature slice of FW = 64, 128 or 256 features) and
 // runs on its own, no block-wide barrier.  The window's stream - its blocks,
 // then the CSR entries of its rows - is consumed in chunks of 16 entries:
 //  * gathers: the 16 B-row slices of a chunk go by 16-byte cp.async into the
@@ -725,13 +725,19 @@ bool window_warp_eligible(const WindowArgs &a, int dtype)
 }
 
 // Launch shape for measurement, read at every launch: SPMM_B200_WW =
-// <FW>s<stages>w<warps per CTA>.  The default (128 or 64 features, 3
-// stages, 4 warps, 3 or 5 CTAs per SM) measured fastest on configs 2 and 3.
+// <FW>s<stages>w<warps per CTA>.  The default is the widest slice the width
+// allows with 3 stages and 4 warps per CTA: 256 features (2 CTAs, 8 warps
+// per SM, 244 registers), else 128 (3 CTAs) or 64 (5 CTAs).  On config 2
+// (N = 256) the 256-feature slice halves the items and doubles the bytes of
+// every chunk: window kernel 462 -> 407 us against 128s3w4 on one box; on
+// config 3 (N = 128) 128s3w4 measured fastest.
 static int ww_variant()
 {
     const char *e = getenv("SPMM_B200_WW");
     if (!e) return 0;
-    static const char *const names[] = {"", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4", "64s3w4"};
+    static const char *const names[] = {"",        "128s4w2", "128s5w2", "128s6w2", "128s5w1",
+                                        "64s6w2",  "64s5w4",  "128s4w4", "64s3w4",  "256s3w4",
+                                        "256s3w2", "256s4w2", "128s3w4"};
     for (int i = 1; i < (int)(sizeof(names) / sizeof(names[0])); ++i)
         if (strcmp(e, names[i]) == 0) return i;
     return 0;
@@ -740,7 +746,7 @@ static int ww_variant()
 template <typename I>
 cudaError_t launch_ww_f16(const WindowArgs &a, cudaStream_t stream)
 {
-    const bool w128 = a.N % 128 == 0;
+    const bool w128 = a.N % 128 == 0, w256 = a.N % 256 == 0;
     switch (ww_variant()) {
     case 1: if (w128) return launch_ww<I, 128, 4, 2>(a, stream); break;
     case 2: if (w128) return launch_ww<I, 128, 5, 2>(a, stream); break;
@@ -750,8 +756,13 @@ cudaError_t launch_ww_f16(const WindowArgs &a, cudaStream_t stream)
     case 6: return launch_ww<I, 64, 5, 4>(a, stream);
     case 7: if (w128) return launch_ww<I, 128, 4, 4>(a, stream); break;
     case 8: return launch_ww<I, 64, 3, 4>(a, stream);
+    case 9: if (w256) return launch_ww<I, 256, 3, 4>(a, stream); break;
+    case 10: if (w256) return launch_ww<I, 256, 3, 2>(a, stream); break;
+    case 11: if (w256) return launch_ww<I, 256, 4, 2>(a, stream); break;
+    case 12: if (w128) return launch_ww<I, 128, 3, 4>(a, stream); break;
     default: break;
     }
+    if (w256) return launch_ww<I, 256, 3, 4>(a, stream);
     return w128 ? launch_ww<I, 128, 3, 4>(a, stream) : launch_ww<I, 64, 3, 4>(a, stream);
 }
 

@@ -19,7 +19,8 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(bool(os.environ.get("SPMM_B200_WINDOW")), reason="another window kernel forced")]
 
 DEV = "cuda"
-VARIANTS = ["", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4", "64s3w4"]
+VARIANTS = ["", "128s4w2", "128s5w2", "128s6w2", "128s5w1", "64s6w2", "64s5w4", "128s4w4", "64s3w4",
+            "256s3w4", "256s3w2", "256s4w2", "128s3w4"]
 
 
 @pytest.fixture(scope="module")
