@@ -5,7 +5,9 @@ same operator.  A is cut into contiguous row ranges balanced by nonzeros at
 16-row window boundaries (so window layouts built per shard keep whole
 windows), B is replicated on every GPU, and each rank computes its own rows
 with the single-GPU operators - there is no communication in the SpMM
-itself.  C stays row-sharded; when a caller asks for the full C on every
+itself.  For the mixed (window + CSR) operator each rank runs the
+reference's task mapping on its own row slice (``ShardedMixed``), so the
+window/CSR decisions stay local to the shard.  C stays row-sharded; when a caller asks for the full C on every
 rank, ``MulticastRows`` fuses the gather into the SpMM (each finished row is
 stored once through an NVLink multicast address and the NVSwitch writes it
 into every GPU's copy while the kernel runs), and ``allgather_rows``
@@ -310,3 +312,64 @@ def spmm_csr_sharded(rowptr, col, val, dense, rank: int, world: int, gather: boo
     if not gather:
         return local, (r0, r1)
     return allgather_rows(local, bounds, group, timeout_s=timeout_s), (0, M)
+
+
+class ShardedMixed:
+    """This rank's rows of ``A @ B`` through the mixed (window + CSR)
+    operator ``spmm_ascend_cube``, with the layout built per shard.
+
+    The rows of A are cut by ``shard_bounds`` (nonzero-balanced, on 16-row
+    window boundaries) and the rank runs ``preprocess`` - the reference's task
+    mapping (extension/custom_op.cpp:765-1137) - on its own row slice only,
+    so every window and every AIC/AIV decision is local to the shard and no
+    rank ever holds another rank's layout.  The layout is built once, at
+    construction; each call runs the operator on the given dense operand,
+    restores the shard's rows to original order (the layout's
+    ``inv_permutation``) and, with ``gather=True``, assembles the full C on
+    every rank with ``allgather_rows`` (NCCL; bounded by ``timeout_s``).
+
+    ``A`` (``rowptr``, ``col``, ``val``) may live on the CPU or the GPU; the
+    layout is built on the current CUDA device.  An empty shard (more ranks
+    than windows) computes nothing and contributes no rows.
+    """
+
+    KEYS = ("crow_window_ptr", "unique_col_ids", "value", "vrow_window_ptr", "vcol_indices", "vvalue")
+
+    def __init__(self, rowptr, col, val, ncols: int, rank: int, world: int, device=None):
+        import spmm_npu
+
+        self.bounds = shard_bounds(rowptr, world)
+        self.r0, self.r1 = self.bounds[rank]
+        self.rows = rowptr.numel() - 1
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.layout = None
+        if self.r1 > self.r0:
+            rp, c, v = shard_csr(rowptr, col, val, self.r0, self.r1)
+            m = spmm_npu.preprocess(rp.to(self.device), c.to(self.device), v.to(self.device), self.r1 - self.r0,
+                                    int(ncols), WINDOW, False)
+            self.layout = [m[k] for k in self.KEYS]
+            self.inv_permutation = m["inv_permutation"]
+            self.packed_rows = int(m["packed_rows"].item())
+        self._cstart = torch.zeros(20, dtype=torch.int32, device=self.device)
+        self._vstart = torch.zeros(40, dtype=torch.int32, device=self.device)
+
+    def packed(self, dense: torch.Tensor) -> torch.Tensor:
+        """The shard's rows in the layout's packed order (the operator's own output)."""
+        import spmm_npu
+
+        if self.layout is None:
+            return dense.new_empty((0, dense.shape[1]))
+        return spmm_npu.spmm_ascend_cube(*self.layout, dense, self._cstart, self._vstart)
+
+    def __call__(self, dense: torch.Tensor, gather: bool = False, group=None, timeout_s: float | None = None):
+        """``(rows, (r0, r1))``: the shard's rows of C in original order, or
+        with ``gather=True`` the full C on every rank and ``(0, rows)``."""
+        import spmm_npu
+
+        if self.layout is None:
+            local = dense.new_empty((0, dense.shape[1]))
+        else:
+            local = spmm_npu.restore_node_tensor(self.packed(dense), self.inv_permutation)
+        if not gather:
+            return local, (self.r0, self.r1)
+        return allgather_rows(local, self.bounds, group, timeout_s=timeout_s), (0, self.rows)

@@ -1,6 +1,8 @@
 """Row-sharded SpMM on 2 GPUs (NCCL): every rank computes its shard with the
-engine's CSR operator, the all-gather assembles C, and the result matches the
-float64 oracle.  Runs as child processes; skipped with fewer than 2 GPUs."""
+engine's CSR operator, and with the mixed operator on a layout built from
+its own rows (ShardedMixed), the all-gather assembles C, and both results
+match the float64 oracle.  Runs as child processes; skipped with fewer than
+2 GPUs."""
 
 import os
 import socket
@@ -31,7 +33,7 @@ def _rank(rank, world, port, q):
     import torch.distributed as dist
 
     import workloads
-    from spmm_dist import spmm_csr_sharded
+    from spmm_dist import ShardedMixed, spmm_csr_sharded
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -40,9 +42,11 @@ def _rank(rank, world, port, q):
     try:
         w = workloads.make(2, scale=0.02, device=f"cuda:{rank}")
         full, _ = spmm_csr_sharded(w.rowptr, w.col, w.val, w.B, rank, world, gather=True)
+        mixed, rows = ShardedMixed(w.rowptr, w.col, w.val, w.K, rank, world)(w.B, gather=True, timeout_s=60.0)
         torch.cuda.synchronize()
+        assert rows == (0, w.M)
         if rank == 0:
-            q.put(full.cpu())
+            q.put((full.cpu(), mixed.cpu()))
     finally:
         dist.destroy_process_group()
 
@@ -60,13 +64,14 @@ def test_two_gpu_row_sharded_spmm():
     procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    full = q.get(timeout=300)
+    full, mixed = q.get(timeout=300)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
     w = workloads.make(2, scale=0.02, device="cuda:0")
     ref = oracle.spmm_csr_f64(w.rowptr.cpu(), w.col.cpu(), w.val.cpu(), w.B.cpu())
     assert_close(full, ref, torch.float16, "2-GPU sharded")
+    assert_close(mixed, ref, torch.float16, "2-GPU sharded mixed (per-shard task mapping)")
 
 
 def _multicast_rank(rank, world, port, q):
