@@ -76,7 +76,7 @@ def parse_args(argv=None):
     p.add_argument("--scale", type=float, default=1.0)
     p.add_argument("--op", choices=("csr", "mixed", "preprocess"), default="csr")
     p.add_argument("--scaling", choices=("strong", "weak"), default="strong")
-    p.add_argument("--e2e-steps", type=int, default=8)
+    p.add_argument("--e2e-steps", type=int, default=16)
     p.add_argument("--e2e-outputs", type=int, choices=(1, 2), default=2,
                    help="device outputs in the e2e pipeline (1: a step's kernel waits for the previous read-back)")
     p.add_argument("--preprocess-config", type=int, default=2)
