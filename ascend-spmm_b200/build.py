@@ -33,7 +33,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
               f"-I{INCLUDE}"]
 
-CU_SOURCES = ["status.cu", "gather.cu", "gather_mma.cu", "window.cu", "window_warp.cu", "window_tc.cu", "rows.cu", "cube.cu", "preprocess.cu", "noalloc.cu", "capi.cu"]
+CU_SOURCES = ["status.cu", "gather.cu", "gather_mma.cu", "window.cu", "window_warp.cu", "window_tc.cu", "rows.cu", "cube.cu", "preprocess.cu", "noalloc.cu", "l2plan.cu", "capi.cu"]
 HEADERS = ["common.cuh", "engine.h"]
 
 

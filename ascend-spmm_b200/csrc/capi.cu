@@ -93,7 +93,7 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
         return set_error(SPMM_ERR_ARG, "%s: workspace must be 16-byte aligned", op);
     if (misaligned(out_mc))
         return set_error(SPMM_ERR_ARG, "%s: the multicast address must be 16-byte aligned", op);
-    const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype);
+    const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype, true);
     if (workspace_bytes < plan.workspace_bytes() || !workspace)
         return set_error(SPMM_ERR_WORKSPACE, "%s: workspace of %zu bytes is smaller than the %zu required", op,
                          workspace_bytes, plan.workspace_bytes());
@@ -107,6 +107,11 @@ int csr_impl(const void *rowptr, const void *col, const void *value, const void 
     spmmb::set_workspace(a, plan, workspace);
     a.out_mc = out_mc;
     a.status = st;
+    if (plan.l2) {   // hot B rows kept in L2 for the ring kernel (cache priorities only)
+        e = spmmb::launch_l2_plan(a, itype, dtype, static_cast<char *>(workspace) + plan.l2_offset(),
+                                  static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_error(e, op);
+    }
     e = spmmb::launch_gather(a, itype, dtype, batch_depth, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_error(e, op);
     return SPMM_OK;
@@ -289,7 +294,14 @@ int spmm_device_status(int *code, int64_t *detail, int reset, void *stream)
 size_t spmm_csr_workspace_bytes(int64_t M, int64_t N, int64_t nnz, int dtype)
 {
     (void)M;
-    return spmmb::plan_gather(nnz, N, dtype).workspace_bytes();
+    return spmmb::plan_gather(nnz, N, dtype, true).workspace_bytes();
+}
+
+size_t spmm_csr_l2_plan_offset(int64_t M, int64_t N, int64_t nnz, int dtype)
+{
+    (void)M;
+    const spmmb::GatherPlan plan = spmmb::plan_gather(nnz, N, dtype, true);
+    return plan.l2 ? plan.l2_offset() : SIZE_MAX;
 }
 
 int spmm_csr_launch(const void *rowptr, const void *col, const void *value, const void *dense,

@@ -53,10 +53,51 @@ struct GatherPlan {
     // each unit for the tensor-core kernel, or the split row of each unit
     // that the ring kernel records for the fix-up
     size_t rows_offset() const { return (partial_bytes() + 255) & ~size_t(255); }
-    size_t workspace_bytes() const { return rows_offset() + (size_t)(nunits() + 1) * sizeof(int64_t); }
+    size_t rows_end() const { return rows_offset() + (size_t)(nunits() + 1) * sizeof(int64_t); }
+    // then, when l2 is set, the L2 residency plan of the B rows (l2plan.cu)
+    bool l2 = false;
+    size_t l2_offset() const { return (rows_end() + 255) & ~size_t(255); }
+    size_t workspace_bytes() const { return l2 ? l2_offset() + l2_plan_bytes() : rows_end(); }
+    static size_t l2_plan_bytes();
 };
 
-GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype);
+// with_l2: reserve the L2 residency plan where l2_plan_wanted() says so
+// (spmm_csr and its variants); the mixed operator and the no-allocation
+// entry point plan without it.
+GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype, bool with_l2 = false);
+
+// ---- L2 residency plan for the B rows (l2plan.cu) ----------------------------
+//
+// For a dense operand far larger than L2 whose columns are skewed (power-law
+// graphs: a few hub rows of B take most of the gathers), L2's replacement
+// lets the long tail of once-used B rows evict the hub rows.  The plan
+// samples the column indices on the device, marks the hottest columns that
+// fit in half of L2 (a bitmap over column ids modulo kL2Bins) and, when the
+// marked columns hold at least a quarter of the samples (l2_plan_enabled),
+// the ring kernel copies their B rows with an evict_last L2 policy and every
+// other B row with evict_first.  Only cache priorities change: results are
+// bitwise the same with or without the plan.
+constexpr int64_t kL2Bins = int64_t(1) << 24;
+struct L2PlanHeader {
+    unsigned threshold;      // a bin is hot when its sample count is at least this (0: none)
+    unsigned hot_bins;       // bins at or above the threshold (the budget bounds them)
+    unsigned budget;         // hot bins allowed: half of L2 in B rows
+    unsigned pad;
+    unsigned long long samples;      // column indices sampled
+    unsigned long long hot_samples;  // of which in hot bins (exact)
+    unsigned hist[1024];     // bins by sample count (capped at 1023)
+};
+static_assert(offsetof(L2PlanHeader, samples) == offsetof(spmm_l2_plan_header, samples) &&
+                  offsetof(L2PlanHeader, hot_samples) == offsetof(spmm_l2_plan_header, hot_samples),
+              "the public header mirrors the plan's first fields");
+__host__ __device__ inline bool l2_plan_enabled(const L2PlanHeader &h)
+{
+    return h.threshold > 0 && h.samples > 0 && 4 * h.hot_samples >= h.samples;
+}
+// Whether a spmm_csr problem reserves the plan in its workspace: rows of at
+// least 1 KB and at least 2^26 nonzeros; SPMM_B200_L2PLAN=on reserves it for
+// every problem with 1 KB rows, =off never.
+bool l2_plan_wanted(int64_t nnz, int64_t N, int dtype);
 
 struct GatherArgs {
     const void *rowptr;
@@ -85,7 +126,17 @@ struct GatherArgs {
     // writes it into each GPU's copy bound to the multicast object; `out`
     // itself is not written directly.  nullptr: plain stores to `out`.
     void *out_mc;
+    // Optional L2 residency plan (launch_l2_plan): hot-column bitmap and its
+    // header; the ring kernel with rows of 1 KB or more uses them.
+    const unsigned *l2_bits;
+    const L2PlanHeader *l2_hdr;
 };
+
+// Runs the L2 plan into `region` (GatherPlan::l2_plan_bytes() bytes) on
+// `stream` when the dense operand is at least 16x L2 (SPMM_B200_L2PLAN=on:
+// always) and the column ids fit in 31 bits; sets a.l2_bits / a.l2_hdr,
+// else leaves them null.
+cudaError_t launch_l2_plan(GatherArgs &a, int itype, int dtype, void *region, cudaStream_t stream);
 
 // Points a's scratch arrays into a workspace of plan.workspace_bytes().
 inline void set_workspace(GatherArgs &a, const GatherPlan &plan, void *ws)

@@ -443,6 +443,30 @@ __device__ __forceinline__ void cp_async16_cg_s(unsigned saddr, const void *gmem
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gmem) : "memory");
 }
+// The same copy with an L2 eviction policy (createpolicy) for the line.
+__device__ __forceinline__ void cp_async16_cg_hint(unsigned saddr, const void *gmem, uint64_t pol)
+{
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(gmem), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_last()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_normal()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
 __device__ __forceinline__ uint4 lds16(unsigned saddr)
 {
     uint4 v;
@@ -535,7 +559,11 @@ __device__ __forceinline__ void lds_words(const void *p, unsigned (&w)[NW])
     }
 }
 
-template <typename T, typename I, int G, int VPL, int U, int MINB, bool FULL>
+// L2H: copies of B rows carry the L2 residency plan's eviction priorities
+// (evict_last for hot columns, evict_first for the rest; the normal priority
+// for all when the plan is not enabled).  The plan's hot bit travels in bit
+// 31 of the staged column index (column ids fit in 31 bits under a plan).
+template <typename T, typename I, int G, int VPL, int U, int MINB, bool FULL, bool L2H = false>
 __global__ void __launch_bounds__(kGatherThreads, MINB)
 csr_ring_kernel(const GatherArgs a)
 {
@@ -567,6 +595,15 @@ csr_ring_kernel(const GatherArgs a)
     const uint4 *Bl = static_cast<const uint4 *>(a.B) + gl;
     uint4 *out = static_cast<uint4 *>(a.out);
     const int NV = (int)(a.N / EPV);
+    uint64_t pol_hot = 0, pol_cold = 0;
+    if constexpr (L2H) {
+        if (l2_plan_enabled(*a.l2_hdr)) {
+            pol_hot = l2_policy_last();
+            pol_cold = l2_policy_first();
+        } else {
+            pol_hot = pol_cold = l2_policy_normal();
+        }
+    }
 
     for (int64_t u = a.unit_begin + stream; u < a.unit_end; u += nstreams) {
         const int64_t lo = u * a.unit;
@@ -686,7 +723,12 @@ csr_ring_kernel(const GatherArgs a)
         auto stage = [&](int slot, const int *cc, const Scalar *vv) {
 #pragma unroll
             for (int k = 0; k < PER; ++k) {
-                s_col[slot * CH + gl + k * G] = cc[k];
+                int c = cc[k];
+                if constexpr (L2H) {   // the plan's hot bit of this column rides in bit 31
+                    const unsigned bin = (unsigned)c & (unsigned)(kL2Bins - 1);
+                    c |= (int)(((__ldg(a.l2_bits + (bin >> 5)) >> (bin & 31u)) & 1u) << 31);
+                }
+                s_col[slot * CH + gl + k * G] = c;
                 s_val[slot * CH + gl + k * G] = vv[k];
             }
         };
@@ -712,25 +754,30 @@ csr_ring_kernel(const GatherArgs a)
                 unsigned cw[U];
                 lds_words<U>(s_col + ((o0 / CH) & 1) * CH + (o0 % CH), cw);
                 const unsigned slot0 = ring_s + (unsigned)((k & 1) * U * VPL * G * 16);
-                if (nv == U) {
+                // one B row: this lane's VPL pieces of it (under L2H with the
+                // plan's policy; bit 31 of the staged index is the hot bit)
+                auto copy_row = [&](int j) {
+                    if constexpr (L2H) {
+                        const uint4 *src = Bl + (int64_t)(int)(cw[j] & 0x7fffffffu) * NV;
+                        const uint64_t pol = (cw[j] >> 31) ? pol_hot : pol_cold;
 #pragma unroll
-                    for (int j = 0; j < U; ++j) {
+                        for (int q = 0; q < VPL; ++q)
+                            if (FULL || gl + q * G < NV)
+                                cp_async16_cg_hint(slot0 + (j * VPL + q) * G * 16, src + q * G, pol);
+                    } else {
                         const uint4 *src = Bl + (int64_t)(int)cw[j] * NV;
 #pragma unroll
                         for (int q = 0; q < VPL; ++q)
                             if (FULL || gl + q * G < NV) cp_async16_cg_s(slot0 + (j * VPL + q) * G * 16, src + q * G);
                     }
+                };
+                if (nv == U) {
+#pragma unroll
+                    for (int j = 0; j < U; ++j) copy_row(j);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < U; ++j) {
-                        if (j < nv) {
-                            const uint4 *src = Bl + (int64_t)(int)cw[j] * NV;
-#pragma unroll
-                            for (int q = 0; q < VPL; ++q)
-                                if (FULL || gl + q * G < NV)
-                                    cp_async16_cg_s(slot0 + (j * VPL + q) * G * 16, src + q * G);
-                        }
-                    }
+                    for (int j = 0; j < U; ++j)
+                        if (j < nv) copy_row(j);
                 }
             }
             cp_async_commit_group();
@@ -977,6 +1024,11 @@ cudaError_t launch_cfg(const GatherArgs &a, cudaStream_t stream)
             // vectors per lane, 8 warps per block
             const size_t smem = (size_t)(kGatherThreads / 32) * RingShape<T, VPL, U>::kWarpBytes;
             constexpr int RMINB = (VPL == 1) ? 3 : 2;
+            if constexpr (VPL >= 2) {   // rows of 1 KB or more: the L2 plan applies
+                if (full && a.l2_bits)
+                    return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, true, true>, a, 32 / G, smem,
+                                             stream);
+            }
             if (full)
                 return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, true>, a, 32 / G, smem, stream);
             return launch_ring<T, I>(csr_ring_kernel<T, I, G, VPL, U, RMINB, false>, a, 32 / G, smem, stream);
@@ -1023,10 +1075,10 @@ cudaError_t launch_typed(const GatherArgs &a, int batch_depth, cudaStream_t s)
 
 }  // namespace
 
-GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype)
+GatherPlan plan_gather(int64_t nnz, int64_t N, int dtype, bool with_l2)
 {
-    (void)dtype;
     GatherPlan p;
+    p.l2 = with_l2 && l2_plan_wanted(nnz, N, dtype);
     p.N = N;
     // Unit size depends on nnz only (never on N, the device or the variant):
     // about 32K units, 256..8192 nonzeros each, a power of two; below 2^20

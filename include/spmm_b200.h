@@ -84,6 +84,27 @@ int spmm_csr_launch(const void *rowptr, const void *col, const void *value,
                     int itype, int dtype, void *workspace, size_t workspace_bytes,
                     void *stream);
 
+/* L2 residency plan of spmm_csr_launch (no counterpart in the reference:
+ * the 910B's gathers have no L2 eviction priorities).  For rows of B of at
+ * least 1 KB, a dense operand of at least 16x the L2 size and at least 2^26
+ * nonzeros (SPMM_B200_L2PLAN=on: any size, =off: never), the launch first
+ * samples 2^22 column indices on the device, marks the hottest B rows that
+ * fit in half of L2, and - when they hold at least a quarter of the samples
+ * - gathers them with an evict_last L2 policy and the other rows with
+ * evict_first.  Results are bitwise the same either way; the plan lives in
+ * the workspace.  This returns the byte offset of its header inside a
+ * spmm_csr workspace (SIZE_MAX when the problem reserves no plan); after a
+ * launch the header holds: */
+struct spmm_l2_plan_header {
+    uint32_t threshold;      /* a column bin is hot at this many samples (0: none) */
+    uint32_t hot_bins;       /* hot bins (column id modulo 2^24) */
+    uint32_t budget;         /* hot bins allowed: half of L2 in B rows */
+    uint32_t reserved;
+    uint64_t samples;        /* column indices sampled */
+    uint64_t hot_samples;    /* of which in hot bins; enabled when 4x >= samples */
+};
+size_t spmm_csr_l2_plan_offset(int64_t M, int64_t N, int64_t nnz, int dtype);
+
 /* Replaces spmm_csr_aiv_mb_batch_impl_npu (custom_op.cpp:154-187; kernel
  * kernels/op_kernel/spmm_csr_aiv_mb_batch.cpp).  Same math and the same
  * nnz split as spmm_csr_launch (bitwise-identical output); it issues its

@@ -84,3 +84,25 @@ def test_operators_reject_cpu_tensors():
     x = torch.zeros(2, dtype=torch.int32)
     with pytest.raises(RuntimeError, match="must be CUDA tensor"):
         spmm_npu.spmm_csr(x, x[:0], torch.zeros(0, dtype=torch.float16), torch.zeros(4, 16, dtype=torch.float16), x)
+
+
+def test_l2_plan_reserved_only_for_large_problems_with_wide_rows(lib, monkeypatch):
+    # default (auto): 1 KB rows and at least 2^26 nonzeros; nothing else pays
+    # for the plan's workspace
+    monkeypatch.delenv("SPMM_B200_L2PLAN", raising=False)
+    lib.spmm_csr_l2_plan_offset.restype = ctypes.c_size_t
+    lib.spmm_csr_l2_plan_offset.argtypes = [ctypes.c_int64] * 3 + [ctypes.c_int]
+    lib.spmm_csr_workspace_bytes.restype = ctypes.c_size_t
+    lib.spmm_csr_workspace_bytes.argtypes = [ctypes.c_int64] * 3 + [ctypes.c_int]
+    none = ctypes.c_size_t(-1).value
+    for N, nnz, dt in ((512, 1 << 20, 0), (128, 1 << 27, 0), (256, 1 << 20, 1), (128, 1 << 27, 1)):
+        assert lib.spmm_csr_l2_plan_offset(1 << 16, N, nnz, dt) == none
+    for N, nnz, dt in ((1024, 1 << 27, 0), (256, 1 << 26, 1)):
+        off = lib.spmm_csr_l2_plan_offset(1 << 16, N, nnz, dt)
+        total = lib.spmm_csr_workspace_bytes(1 << 16, N, nnz, dt)
+        assert off != none and off % 256 == 0 and total - off > (1 << 26)
+    monkeypatch.setenv("SPMM_B200_L2PLAN", "off")
+    assert lib.spmm_csr_l2_plan_offset(1 << 16, 1024, 1 << 27, 0) == none
+    monkeypatch.setenv("SPMM_B200_L2PLAN", "on")
+    assert lib.spmm_csr_l2_plan_offset(1 << 16, 512, 1 << 10, 0) != none
+    assert lib.spmm_csr_l2_plan_offset(1 << 16, 256, 1 << 10, 0) == none   # 512-byte rows: never
