@@ -71,12 +71,20 @@ __global__ void __launch_bounds__(256) l2_sample_kernel(const I *col, int64_t nn
     }
     __syncthreads();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    constexpr int kIlp = 4;   // independent column loads in flight per thread
     unsigned long long taken = 0;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < S; i += stride) {
-        const int64_t p = i * nnz / S;   // i < 2^22 and nnz < 2^40: no overflow
-        const int64_t c = (int64_t)ld_stream(col + p);
-        if (c >= 0 && c < K) {
-            const int bin = (int)(c & (kL2Bins - 1));
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < S; i0 += kIlp * stride) {
+        int64_t c[kIlp];
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u) {
+            const int64_t i = i0 + u * stride;
+            // i < 2^22 and nnz < 2^40: no overflow
+            c[u] = i < S ? (int64_t)ld_stream(col + i * nnz / S) : int64_t(-1);
+        }
+#pragma unroll
+        for (int u = 0; u < kIlp; ++u) {
+            if (c[u] < 0 || c[u] >= K) continue;
+            const int bin = (int)(c[u] & (kL2Bins - 1));
             const int slot = (int)(((unsigned)bin * 2654435761u) >> 20);   // 12 bits
             int k = s_key[slot];
             if (k < 0) {

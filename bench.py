@@ -223,6 +223,45 @@ def traffic_per_launch(key: str, units: float):
         return None, None
 
 
+def l2_plan_probe(rp, col, val, B, out):
+    """The L2 residency plan of one spmm_csr launch (untimed), read back
+    through the C ABI: whether this problem reserves a plan, whether it
+    engaged (hot columns hold at least a quarter of the sampled nonzeros),
+    the hot column bins and their share of the samples.  ``out`` receives
+    the product (the same bits as the timed steps)."""
+    import ctypes
+
+    import build
+
+    L = ctypes.CDLL(str(build.LIB))
+    V, I64, INT, SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+    L.spmm_csr_l2_plan_offset.restype = SZ
+    L.spmm_csr_l2_plan_offset.argtypes = [I64, I64, I64, INT]
+    L.spmm_csr_workspace_bytes.restype = SZ
+    L.spmm_csr_workspace_bytes.argtypes = [I64, I64, I64, INT]
+    L.spmm_csr_launch.restype = INT
+    L.spmm_csr_launch.argtypes = [V, V, V, V, V, I64, V, I64, I64, I64, I64, INT, INT, V, SZ, V]
+    M, K, N, nnz = rp.numel() - 1, B.shape[0], B.shape[1], col.numel()
+    dt = 0 if B.dtype == torch.float16 else 1
+    it = 0 if rp.dtype == torch.int32 else 1
+    off = L.spmm_csr_l2_plan_offset(M, N, nnz, dt)
+    if off == ctypes.c_size_t(-1).value:
+        return {"reserved": False, "engaged": False}
+    wb = L.spmm_csr_workspace_bytes(M, N, nnz, dt)
+    ws = torch.empty(wb, dtype=torch.uint8, device=B.device)
+    rc = L.spmm_csr_launch(rp.data_ptr(), col.data_ptr(), val.data_ptr(), B.data_ptr(), None, 0, out.data_ptr(),
+                           M, K, N, nnz, it, dt, ws.data_ptr(), wb, torch.cuda.current_stream().cuda_stream)
+    if rc != 0:
+        return {"reserved": True, "error": rc}
+    h = ws[off: off + 32].cpu().numpy().view("<u4")
+    threshold, hot_bins, budget = int(h[0]), int(h[1]), int(h[2])
+    samples, hot = int(h[4]) | (int(h[5]) << 32), int(h[6]) | (int(h[7]) << 32)
+    del ws
+    return {"reserved": True, "engaged": bool(threshold > 0 and samples > 0 and 4 * hot >= samples),
+            "hot_column_bins": hot_bins, "budget_bins": budget, "threshold_samples": threshold,
+            "samples": samples, "hot_sample_fraction": round(hot / samples, 4) if samples else 0.0}
+
+
 def value_bytes(dtype) -> int:
     return torch.finfo(dtype).bits // 8
 
@@ -535,6 +574,12 @@ def run_ours(args, rank, world, local):
     comp = compulsory_bytes(M_local, col, w.N, s, w.K)
     peak, peak_kind = peak_hbm()
     key = f"{w.name}:{args.op}"
+    l2_plan = None
+    if mixed is None:   # spmm_csr: did the L2 residency plan engage (its traffic was measured apart)
+        l2_plan = l2_plan_probe(rp, col, val, B, step())
+        torch.cuda.synchronize()
+        if not l2_plan.get("engaged"):
+            key += ":no_l2_plan"
     traffic, traffic_src = traffic_per_launch(key, nnz_local)
     roofline = {
         "bound": "hbm", "achieved": round(algo / kernel_s / 1e9, 1), "peak": peak, "unit": "GB/s",
@@ -550,6 +595,8 @@ def run_ours(args, rank, world, local):
         "dram_frac": round(traffic / kernel_s / 1e9 / peak, 4) if traffic else None,
         "traffic_source": traffic_src,
     }
+    if l2_plan is not None:
+        roofline["l2_plan"] = l2_plan
 
     extra = {}
     if args.gather and world > 1:
