@@ -76,12 +76,15 @@ def test_oracle_matches_reference(seed):
     same(oracle.preprocess(ct, cc, vals, nrows, ncols, 16, True), exp["preg"])
 
 
-@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05)])
+@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05), (3, 0.05), (4, 0.02)])
 def test_oracle_matches_reference_at_config_scale(cfg, scale):
     """The restatement against the compiled reference on BASELINE-shaped
     matrices: config 1 at full size (16384 rows, 163840 nonzeros: 1024
     windows, the marginal-window bucket sort and density sorts over all of
-    them) and config 2 at scale 0.05 (power-law, 52428 rows)."""
+    them), config 2 at scale 0.05 (power-law, 52428 rows), config 3 at
+    scale 0.05 (dense 16 x 16 block bands: most nonzeros in windows) and
+    config 4 at scale 0.02 (fp32 values, 64-column clusters beside Poisson
+    rows)."""
     import workloads
 
     r = ref()
