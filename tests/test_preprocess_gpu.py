@@ -213,11 +213,12 @@ def test_gpu_layouts_drive_spmm(npu):
     assert code == 0, (code, detail)
 
 
-@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05)])
+@pytest.mark.parametrize("cfg,scale", [(1, 1.0), (2, 0.05), (3, 0.05), (4, 0.02)])
 def test_layouts_match_compiled_reference(npu, cfg, scale):
     """GPU layouts against the reference's own compiled CPU preprocessing
-    (oracle/_ref, built from the reference tree) on config 1 at full size
-    and config 2 at scale 0.05, graph layout included."""
+    (oracle/_ref, built from the reference tree) on config 1 at full size,
+    config 2 at scale 0.05, config 3 at scale 0.05 and config 4 (fp32) at
+    scale 0.02, graph layout included."""
     import contextlib
     import io
 
