@@ -1,5 +1,5 @@
 """Multi-rank host logic on CPU (gloo, world_size 2): row partition, shard
-slicing and the all-gather of row-sharded C.  The per-rank product is the
+slicing, the all-gather of row-sharded C and the sharded mixed operator.  The per-rank product is the
 float64 oracle here (no GPU); the GPU path is the same code with
 spmm_npu.spmm_csr as the local operator."""
 
@@ -89,6 +89,59 @@ def test_allgather_reassembles_full_product():
         for r in range(world):
             np.testing.assert_allclose(results[r], ref, rtol=0, atol=0)
             np.testing.assert_allclose(results[("even", r)], ref[: 2 * half], rtol=0, atol=0)
+
+
+def _mixed_worker(rank, world, port, results):
+    """ShardedMixed's host logic on gloo: the device operators are replaced
+    by the CPU oracle (layout builder, mixed product) and an index gather
+    (row restore), so sharding, per-shard layouts, the restore to original
+    order and the all-gather are what runs."""
+    import torch.distributed as dist
+
+    import spmm_npu
+    from spmm_dist import ShardedMixed
+
+    spmm_npu.preprocess = oracle.preprocess
+    spmm_npu.spmm_ascend_cube = lambda *a: torch.from_numpy(oracle.spmm_mixed_f64(*a[:7]))
+    spmm_npu.restore_node_tensor = lambda packed, inv: packed[inv.to(torch.long)]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = workloads.make(3, scale=0.01)
+        op = ShardedMixed(w.rowptr, w.col, w.val, w.K, rank, world, device="cpu")
+        local, rows = op(w.B)
+        results[("local", rank)] = (rows, local.numpy())
+        full, rows = op(w.B, gather=True)
+        results[("full", rank)] = (rows, full.numpy())
+        results[("windows", rank)] = int(op.layout[0].numel() - 1)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_mixed_host_logic_two_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_mixed_worker, args=(r, world, port, results)) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=180)
+            assert p.exitcode == 0
+        w = workloads.make(3, scale=0.01)
+        ref = oracle.spmm_csr_f64(w.rowptr, w.col, w.val, w.B)
+        bounds = shard_bounds(w.rowptr, world)
+        for r in range(world):
+            rows, local = results[("local", r)]
+            assert rows == bounds[r] and local.shape == (rows[1] - rows[0], w.N)
+            np.testing.assert_allclose(local, ref[rows[0]:rows[1]], rtol=1e-12, atol=1e-12)
+            rows, full = results[("full", r)]
+            assert rows == (0, w.M)
+            np.testing.assert_allclose(full, ref, rtol=1e-12, atol=1e-12)
+            assert results[("windows", r)] > 0   # each shard has its own window layout
 
 
 # ---------------------------------------------------------------- failure handling
