@@ -11,8 +11,9 @@
 // How, on the caller's stream, all on the device (no host synchronisation):
 //  1. zero the counters and the header (one memset);
 //  2. l2_sample_kernel: S = min(nnz, 2^22) column indices at evenly spaced
-//     positions, one atomic increment per sample on its bin (column id
-//     modulo kL2Bins = 2^24: exact for matrices of up to 16.8M columns);
+//     positions, counted per bin (column id modulo kL2Bins = 2^24: exact
+//     for matrices of up to 16.8M columns), the hub columns in a per-block
+//     shared-memory table first;
 //  3. l2_hist_kernel: histogram of the bins' counts (capped at 1023);
 //  4. l2_select_kernel: the smallest threshold t >= 2 whose bins (count >= t)
 //     fit in the budget - half of L2 in B rows of this width;
@@ -21,8 +22,9 @@
 // The ring kernel reads the header: with at least a quarter of the samples
 // in hot bins (l2_plan_enabled) it copies hot rows with evict_last and the
 // rest with evict_first; otherwise every copy keeps the normal priority.
-// A column sampled once is never hot (t >= 2), so uniform matrices (about
-// one sample per column or fewer) end with no hot bins and plain copies.
+// A column sampled once is never hot (t >= 2); on a uniform matrix the bins
+// that fit the budget hold far less than a quarter of the samples (a test
+// matrix with about two samples per column: 14 %), so the plan stays off.
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
