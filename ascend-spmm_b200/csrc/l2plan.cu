@@ -23,8 +23,9 @@
 // in hot bins (l2_plan_enabled) it copies hot rows with evict_last and the
 // rest with evict_first; otherwise every copy keeps the normal priority.
 // A column sampled once is never hot (t >= 2); on a uniform matrix the bins
-// that fit the budget hold far less than a quarter of the samples (a test
-// matrix with about two samples per column: 14 %), so the plan stays off.
+// that fit the budget hold far less than a quarter of the samples (for
+// about two samples per column, Poisson counts put ~14 % of them in the
+// bins above the threshold), so the plan stays off.
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
