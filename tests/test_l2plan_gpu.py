@@ -41,12 +41,15 @@ def lib():
     L.spmm_csr_l2_plan_offset.argtypes = [I64, I64, I64, INT]
     L.spmm_csr_launch.restype = INT
     L.spmm_csr_launch.argtypes = [V, V, V, V, V, I64, V, I64, I64, I64, I64, INT, INT, V, SZ, V]
+    L.spmm_csr_aiv_mb_batch_launch.restype = INT
+    L.spmm_csr_aiv_mb_batch_launch.argtypes = L.spmm_csr_launch.argtypes
     return L
 
 
-def run(L, rp, col, val, B, mode):
-    """spmm_csr through the C ABI under SPMM_B200_L2PLAN=mode; the output and
-    the plan header (None when the problem reserves no plan)."""
+def run(L, rp, col, val, B, mode, entry="spmm_csr_launch"):
+    """spmm_csr (or another entry point with its signature) through the C
+    ABI under SPMM_B200_L2PLAN=mode; the output and the plan header (None
+    when the problem reserves no plan)."""
     old = os.environ.get("SPMM_B200_L2PLAN")
     os.environ["SPMM_B200_L2PLAN"] = mode
     try:
@@ -57,8 +60,9 @@ def run(L, rp, col, val, B, mode):
         off = L.spmm_csr_l2_plan_offset(M, N, nnz, dt)
         ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
         out = torch.empty(M, N, dtype=B.dtype, device="cuda")
-        rc = L.spmm_csr_launch(rp.data_ptr(), col.data_ptr(), val.data_ptr(), B.data_ptr(), None, 0, out.data_ptr(),
-                               M, K, N, nnz, it, dt, ws.data_ptr(), wb, torch.cuda.current_stream().cuda_stream)
+        rc = getattr(L, entry)(rp.data_ptr(), col.data_ptr(), val.data_ptr(), B.data_ptr(), None, 0,
+                               out.data_ptr(), M, K, N, nnz, it, dt, ws.data_ptr(), wb,
+                               torch.cuda.current_stream().cuda_stream)
         assert rc == 0, L.spmm_last_error()
         torch.cuda.synchronize()
         hdr = None
@@ -103,6 +107,10 @@ def test_power_law_plan_enables_and_keeps_results(lib, dtype, N, idt):
     assert torch.equal(y_plan, y_off), "cache priorities changed the result"
     y_again, _ = run(lib, rp, col, val, B, "on")   # the plan region is rebuilt on every call
     assert torch.equal(y_again, y_off)
+    # the deep-batch ablation variant under the plan: same sums, bit for bit
+    y_deep, h_deep = run(lib, rp, col, val, B, "on", "spmm_csr_aiv_mb_batch_launch")
+    assert h_deep is not None and enabled(h_deep)
+    assert torch.equal(y_deep, y_off)
     check_rows(y_plan, rp, col, val, B)
 
 
