@@ -75,14 +75,16 @@ __global__ void __launch_bounds__(256) l2_sample_kernel(const I *col, int64_t nn
     __syncthreads();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     constexpr int kIlp = 4;   // independent column loads in flight per thread
+    // position of sample i = floor(i * nnz / S), as i * q + floor(i * r / S)
+    // with nnz = q * S + r, so no product exceeds 2^22 * nnz / S or 2^44
+    const int64_t q = nnz / S, r = nnz % S;
     unsigned long long taken = 0;
     for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < S; i0 += kIlp * stride) {
         int64_t c[kIlp];
 #pragma unroll
         for (int u = 0; u < kIlp; ++u) {
             const int64_t i = i0 + u * stride;
-            // i < 2^22 and nnz < 2^40: no overflow
-            c[u] = i < S ? (int64_t)ld_stream(col + i * nnz / S) : int64_t(-1);
+            c[u] = i < S ? (int64_t)ld_stream(col + (i * q + i * r / S)) : int64_t(-1);
         }
 #pragma unroll
         for (int u = 0; u < kIlp; ++u) {
